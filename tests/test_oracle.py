@@ -1,0 +1,52 @@
+"""The CPU oracle against the reference's own outputs (golden fixtures)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as O
+from tests.golden_cases import layer_cases, layer_inputs, routing_cases, routing_inputs
+
+LAYER = layer_cases()
+ROUTING = routing_cases()
+
+
+@pytest.mark.parametrize("name", sorted(LAYER))
+def test_oracle_layer_matches_reference(name):
+    case = LAYER[name]
+    ti, wb, offset, rsf = layer_inputs(case)
+    out, idx, w = O.moe_layer(ti.routing_logits, ti.routing_bias, ti.hidden_states, ti.hidden_states_scale,
+                              wb.gemm1_weights, wb.gemm1_weights_scale, wb.gemm2_weights,
+                              wb.gemm2_weights_scale, offset, rsf, return_routing=True)
+    ids_sorted, _ = idx.sort(dim=1)
+    assert np.array_equal(ids_sorted.numpy(), case["topk_sorted"].astype(np.int64))
+    assert np.array_equal(torch.gather(w, 1, ids_sorted).numpy(), case["topk_weights"])
+    # the restatement performs the same fp32 operations in the same order: bit-exact
+    assert np.array_equal(out.view(torch.int16).numpy(), case["out_bf16"])
+
+
+@pytest.mark.parametrize("name", sorted(ROUTING))
+def test_oracle_routing_matches_reference(name):
+    case = ROUTING[name]
+    ti = routing_inputs(case)
+    idx, w = O.route(ti.routing_logits, ti.routing_bias, 2.5)
+    ids_sorted, _ = idx.sort(dim=1)
+    assert np.array_equal(ids_sorted.numpy(), case["topk_sorted"].astype(np.int64))
+    assert np.array_equal(torch.gather(w, 1, ids_sorted).numpy(), case["topk_weights"])
+
+
+def test_oracle_sort_tokens_is_stable_by_expert():
+    idx = torch.tensor([[3, 1, 40, 2, 0, 5, 6, 7], [1, 3, 9, 10, 11, 12, 13, 33]])
+    sid, sle, starts, counts = O.sort_tokens(idx, 0, 32)
+    assert sle.tolist() == sorted(sle.tolist())
+    # token order inside each expert is ascending (stable argsort of the flat pairs)
+    for e in range(32):
+        seg = sid[int(starts[e]): int(starts[e] + counts[e])].tolist()
+        assert seg == sorted(seg)
+    assert int(counts.sum()) == 14
+
+
+def test_tolerance_checker_rejects_single_fp8_requant_scale_error():
+    ref = torch.linspace(-3, 3, 10000).to(torch.bfloat16)
+    bad = (ref.float() * 1.05).to(torch.bfloat16)
+    assert not O.check_tolerance(bad, ref)["ok"]
+    assert O.check_tolerance(ref, ref)["ok"]
