@@ -1,0 +1,352 @@
+#!/usr/bin/env python
+"""Benchmark of the fused DeepSeek-V3 FP8 block-scale MoE layer on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kernelforge|reference]
+                    [--workload ep|prefill|decode] [--tokens T]
+
+Default workload ("ep", the layer of config 3 of the headline metric): 8192
+tokens per GPU, all 256 experts sharded 256/N per GPU (N=1: all 256 on one GPU),
+hidden 7168 / intermediate 2048 FP8 block-scaled weights; tokens are routed over
+all experts.  With N > 1 the layer runs expert-parallel (one process per GPU,
+launched by torchrun) with NCCL all-to-all dispatch/combine.  A "step" is one
+forward of the layer over the GPU's 8192 tokens; per-GPU work is fixed as N
+grows (weak scaling).
+
+Prints ONE JSON line (rank 0).  Metric: tokens/s of the whole job (all GPUs).
+Inputs are synthetic (seeded N(0,1) logits / activations, N(0,0.02) weights,
+generated on the GPU); the weights (11.3 GB) are far larger than L2, so every
+step streams them from HBM (no L2 flush needed).
+
+--impl reference times the reference algorithm's CPU path (the oracle port of
+solution/triton/kernel.py::kernel's PyTorch loop) on this host's cores, one
+bounded sample (one token) per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+H, I, E_GLOBAL = 7168, 2048, 256
+FLOP_PER_PAIR = 2 * (2 * I * H + H * I)            # 88,080,384
+GEMM1_FLOP_PER_PAIR = 2 * 2 * I * H                # 58,720,256
+METRIC = "MoE layer tokens/s (FP8 block-scale DeepSeek-V3 layer, T=8192 tokens per GPU, 256 experts EP-sharded)"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="kernelforge", choices=["kernelforge", "reference"])
+    p.add_argument("--workload", default="ep", choices=["ep", "prefill", "decode"])
+    p.add_argument("--tokens", type=int, default=None)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16": d["bf16_tflops"], "bf16_sustained": d["bf16_tflops_sustained"],
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi samples (every 200 ms) of the SM clock and throttle reasons during the timed region."""
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples = []
+        self._proc = None
+        self._thread = None
+
+    def start(self):
+        cmd = ["nvidia-smi", "-i", str(self.gpu),
+               "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+               "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "200"]
+        try:
+            self._proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self._proc = None
+            return
+        self._thread = threading.Thread(target=self._read, daemon=True)
+        self._thread.start()
+
+    def _read(self):
+        for line in self._proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 7:
+                self.samples.append((time.time(), parts))
+
+    def stop(self):
+        if self._proc is not None:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+        if self._thread is not None:
+            self._thread.join(timeout=5)
+
+    def summary(self, t0: float, t1: float):
+        window = [p for (t, p) in self.samples if t0 <= t <= t1] or [p for (_, p) in self.samples]
+        if not window:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        mhz = [float(p[0]) for p in window if p[0].replace(".", "").isdigit()]
+        mx = [float(p[1]) for p in window if p[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for p in window for i in range(4) if p[3 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(window)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def workload_shape(args, world):
+    if args.workload == "ep":
+        T = args.tokens or 8192
+        E = E_GLOBAL // world
+        return T, E, "ep_layer_T8192_per_gpu_256_experts" if T == 8192 else f"ep_layer_T{T}_per_gpu_256_experts"
+    if args.workload == "prefill":
+        T = args.tokens or 4096
+        return T, 32, f"prefill_T{T}_32_local_experts"
+    T = args.tokens or 16
+    return T, 32, f"decode_T{T}_32_local_experts"
+
+
+# ---------------------------------------------------------------- CPU baseline --
+def cpu_oracle_tokens_per_s(tokens: int, seed: int = 0):
+    """The oracle (reference algorithm, PyTorch CPU) on `tokens` tokens of the workload.
+
+    Only the experts those tokens reach are materialised (in a compact bank); the
+    timed part is the reference's own work: routing, per-expert dequantisation,
+    fp32 GEMMs, SwiGLU and the weighted index_add combine.
+    """
+    from kernelforge_b200 import synthetic as S
+    from oracle import moe_oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    ti = S.token_inputs(tokens, seed=seed + 1000)
+    idx, _ = O.route(ti.routing_logits, ti.routing_bias, 2.5)
+    active = sorted(set(idx.flatten().tolist()))
+    banks = [S.expert_weights(g, seed=0) for g in active]
+    w13 = torch.stack([b[0] for b in banks]); w13s = torch.stack([b[1] for b in banks])
+    w2 = torch.stack([b[2] for b in banks]); w2s = torch.stack([b[3] for b in banks])
+    lut = torch.full((E_GLOBAL,), -1, dtype=torch.int64)
+    lut[torch.tensor(active)] = torch.arange(len(active))
+    t0 = time.perf_counter()
+    idx, w = O.route(ti.routing_logits, ti.routing_bias, 2.5)
+    cidx = lut[idx]
+    wsel = torch.gather(w, 1, idx)
+    out = O.moe_experts(cidx, wsel, ti.hidden_states, ti.hidden_states_scale, w13, w13s, w2, w2s, 0)
+    out = out.to(torch.bfloat16)
+    dt = time.perf_counter() - t0
+    return tokens / dt, dt, len(active)
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    T, E, name = workload_shape(args, 1)
+    cores = torch.get_num_threads() if False else (os.cpu_count() or 1)
+    for _ in range(args.warmup):
+        cpu_oracle_tokens_per_s(1, seed=7)
+    times = []
+    t_all = 0.0
+    for k in range(args.steps):
+        _, dt, _ = cpu_oracle_tokens_per_s(1, seed=100 + k)
+        times.append(dt)
+        t_all += dt
+    value = args.steps / t_all
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t_all / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": name, "tokens_per_gpu": T, "experts": E_GLOBAL, "sample": "1 token per step"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": "1 token of the workload per step through its 8 experts (PyTorch CPU, "
+                                   "reference algorithm restated in oracle/moe_oracle.py)"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------- our arm --
+def main():
+    args = parse()
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
+
+    from kernelforge_b200 import binding as B
+    from kernelforge_b200 import synthetic as S
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    T, E, name = workload_shape(args, world)
+    offset = rank * E if args.workload == "ep" else 0
+    peaks = load_peaks()
+
+    ti = S.token_inputs(T, seed=17 + rank, device=dev)
+    wb = S.expert_bank(E, offset, seed=0, device=dev)
+    torch.cuda.synchronize(dev)
+
+    if world > 1:
+        from kernelforge_b200 import ep
+        layer = ep.ExpertParallelMoE(wb, offset, E)
+
+        def step(logits, bias, hid, hs):
+            return layer.forward(logits, bias, hid, hs, 2.5)
+    else:
+        def step(logits, bias, hid, hs):
+            return B.kernel(logits, bias, hid, hs, wb.gemm1_weights, wb.gemm1_weights_scale, wb.gemm2_weights,
+                            wb.gemm2_weights_scale, offset, 2.5)
+
+    # local (token, expert) pairs of this rank's GEMMs (for the FLOP count)
+    idx, _ = B.route(ti.routing_logits, ti.routing_bias, 2.5)
+    pairs = int(((idx >= offset) & (idx < offset + E)).sum().item()) if world == 1 else None
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    for _ in range(args.warmup):
+        step(ti.routing_logits, ti.routing_bias, ti.hidden_states, ti.hidden_states_scale)
+    torch.cuda.synchronize(dev)
+
+    clocks = ClockSampler(dev.index if world == 1 else local)
+    clocks.start()
+    time.sleep(0.5)
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    step_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize(dev)
+    B.profile_begin()
+    t_wall0 = time.time()
+    ev0.record(stream)
+    for k in range(args.steps):
+        step_ev[k][0].record(stream)
+        step(ti.routing_logits, ti.routing_bias, ti.hidden_states, ti.hidden_states_scale)
+        step_ev[k][1].record(stream)
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    t_wall1 = time.time()
+    prof = B.profile_end()
+    barrier()
+    clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    step_ms = sorted(a.elapsed_time(b) for a, b in step_ev)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = world * T * args.steps / (ms / 1e3)
+
+    # end to end through the public API: per-step inputs from pinned host memory, result back to host
+    e2e = None
+    h_logits = ti.routing_logits.cpu().pin_memory()
+    h_bias = ti.routing_bias.cpu().pin_memory()
+    h_hid = ti.hidden_states.cpu().pin_memory()
+    h_hs = ti.hidden_states_scale.cpu().pin_memory()
+    h_out = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
+    d_logits, d_bias = torch.empty_like(ti.routing_logits), torch.empty_like(ti.routing_bias)
+    d_hid, d_hs = torch.empty_like(ti.hidden_states), torch.empty_like(ti.hidden_states_scale)
+    h2d = sum(t.numel() * t.element_size() for t in (h_logits, h_bias, h_hid, h_hs))
+    d2h = h_out.numel() * h_out.element_size()
+    e2e_steps = max(3, min(args.steps, 20))
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        d_logits.copy_(h_logits, non_blocking=True)
+        d_bias.copy_(h_bias, non_blocking=True)
+        d_hid.copy_(h_hid, non_blocking=True)
+        d_hs.copy_(h_hs, non_blocking=True)
+        o = step(d_logits, d_bias, d_hid, d_hs)
+        h_out.copy_(o, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e_ms = float(t.item())
+    e2e = {"value": world * T * e2e_steps / (e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+           "d2h_bytes_per_step": d2h, "steps": e2e_steps}
+
+    # roofline of the dominant kernel (GEMM1: 2/3 of the layer's FLOPs)
+    g1_ms, g1_n = prof["gemm1_swiglu"]
+    g2_ms, g2_n = prof["gemm2_weighted"]
+    total_launches = sum(n for _, n in prof.values())
+    roofline = None
+    if g1_n and pairs is not None:
+        g1_avg = g1_ms / g1_n
+        achieved = GEMM1_FLOP_PER_PAIR * pairs / (g1_avg / 1e3) / 1e12
+        peak = 2.0 * peaks["bf16_sustained"]
+        roofline = {"bound": "tensor", "kernel": "gemm1_swiglu", "achieved": achieved, "peak": peak,
+                    "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                    "peak_note": f"FP8 dense = 2 x {peaks['source']} sustained cuBLAS bf16 "
+                                 f"({peaks['bf16_sustained']} TFLOP/s)",
+                    "avg_launch_ms": g1_avg}
+    kernels = {k: {"ms_per_launch": (v[0] / v[1]) if v[1] else None, "launches": v[1],
+                   "share": (v[0] / sum(x[0] for x in prof.values())) if v[1] else 0.0}
+               for k, v in prof.items()}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tps, dt, nact = cpu_oracle_tokens_per_s(8, seed=0)
+        cpu = {"value": tps, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+               "sample": f"8 tokens of the workload through their {nact} experts (PyTorch CPU, "
+                         f"{dt:.1f} s; reference algorithm restated in oracle/moe_oracle.py)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp8_e4m3 (fp32 accumulate)", "data": "synthetic",
+            "config": {"workload": name, "tokens_per_gpu": T, "local_experts_per_gpu": E,
+                       "global_experts": E_GLOBAL, "hidden": H, "intermediate": I, "top_k": 8,
+                       "parallelism": f"ep{world}", "l2": "inputs larger than L2 (weights stream from HBM)",
+                       "pairs_rank0": pairs},
+            "p50_step_ms": step_ms[len(step_ms) // 2], "p90_step_ms": step_ms[int(len(step_ms) * 0.9)],
+            "tflops_per_gpu": (FLOP_PER_PAIR * pairs / (ms_per_step / 1e3) / 1e12) if pairs else None,
+            "roofline": roofline, "kernels": kernels, "gpu_launches": total_launches,
+            "e2e": e2e, "cpu_baseline": cpu,
+            "clocks": clocks.summary(t_wall0, t_wall1),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

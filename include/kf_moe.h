@@ -1,0 +1,151 @@
+/*
+ * kf_moe.h -- C ABI of the B200 (sm_100a) fused DeepSeek-V3 FP8 block-scale MoE layer.
+ *
+ * Definition: moe_fp8_block_scale_ds_routing_topk8_ng8_kg4_e32_h7168_i2048
+ * (hidden 7168, intermediate 2048, 256 global experts in 8 groups of 32, top-4
+ * groups, top-8 experts, FP8 e4m3 operands with fp32 scales per 128 columns of
+ * activations and per 128x128 block of weights).
+ *
+ * The entry points replace the reference's Python operator
+ * ``solution/triton/kernel.py::kernel`` (chinmay29/kernelforge):
+ *
+ *   kf_moe_forward  <- kernel(...)                       kernel.py:1817-1950
+ *   kf_moe_route    <- routing inside kernel(...)         kernel.py:1842-1867
+ *                      (= _route_topk_ids_and_weights     kernel.py:967-993)
+ *   kf_moe_experts  <- sort + grouped GEMM1/SwiGLU +      kernel.py:1869-1925
+ *                      grouped GEMM2 + index_add combine  (_sort_tokens :46-82,
+ *                                                          _launch_grouped_gemm1_swiglu :626,
+ *                                                          _launch_grouped_gemm2 :688)
+ *
+ * All pointers are device pointers (except where noted), all tensors are dense
+ * row-major, and every call is asynchronous on `stream` (a cudaStream_t, NULL =
+ * legacy default stream).  Calls never synchronise the host and never allocate:
+ * scratch memory is the caller's `workspace` of kf_moe_workspace_bytes() bytes.
+ * Return value: KF_OK or a KF_ERR_* code (argument / launch errors only; errors
+ * found on the device are reported through kf_moe_read_status).
+ */
+#ifndef KF_MOE_H_
+#define KF_MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KF_MOE_HIDDEN 7168
+#define KF_MOE_INTERMEDIATE 2048
+#define KF_MOE_GLOBAL_EXPERTS 256
+#define KF_MOE_TOP_K 8
+#define KF_MOE_N_GROUP 8
+#define KF_MOE_TOPK_GROUP 4
+#define KF_MOE_BLOCK 128
+
+/* Host-side return codes. */
+#define KF_OK 0
+#define KF_ERR_INVALID_ARGUMENT 1
+#define KF_ERR_WORKSPACE_TOO_SMALL 2
+#define KF_ERR_CUDA 3
+#define KF_ERR_UNSUPPORTED_DEVICE 4
+#define KF_ERR_DRIVER_ENTRY_POINT 5
+#define KF_ERR_DEVICE_STATUS 6
+
+/* Device status bits (OR-ed into the workspace status word by the kernels). */
+#define KF_STATUS_TIMEOUT_PRODUCER 0x01 /* a TMA producer waited too long for a free stage */
+#define KF_STATUS_TIMEOUT_MMA 0x02      /* the MMA issuer waited too long for data / TMEM */
+#define KF_STATUS_TIMEOUT_EPILOGUE 0x04 /* a promotion/epilogue warp waited too long */
+#define KF_STATUS_BAD_EXPERT 0x08       /* a routed expert id outside [0, 256) */
+#define KF_STATUS_SLOT_OVERFLOW 0x10    /* a permuted row index beyond the workspace capacity */
+
+/*
+ * Bytes of scratch memory a call with `num_tokens` tokens and `num_local_experts`
+ * local experts needs (sized for the worst case: every token routed to
+ * min(8, E) local experts).  Replaces the torch allocations the reference makes
+ * inside kernel(...).
+ */
+size_t kf_moe_workspace_bytes(int32_t num_tokens, int32_t num_local_experts);
+
+/*
+ * The whole layer, value-returning in the reference; here the caller passes the
+ * output buffer.
+ *   routing_logits      f32  [T, 256]
+ *   routing_bias        bf16 [256]
+ *   hidden_states       e4m3 [T, 7168]
+ *   hidden_states_scale f32  [56, T]
+ *   gemm1_weights       e4m3 [E, 4096, 7168]   rows [0,2048) = up (X1), [2048,4096) = gate (X2)
+ *   gemm1_weights_scale f32  [E, 32, 56]
+ *   gemm2_weights       e4m3 [E, 7168, 2048]
+ *   gemm2_weights_scale f32  [E, 56, 16]
+ *   output              bf16 [T, 7168]
+ * Local experts are global ids [local_expert_offset, local_expert_offset + E);
+ * tokens routed to no local expert produce zero rows.  1 <= E <= 256.
+ */
+int kf_moe_forward(const float* routing_logits, const void* routing_bias,
+                   const void* hidden_states, const float* hidden_states_scale,
+                   const void* gemm1_weights, const float* gemm1_weights_scale,
+                   const void* gemm2_weights, const float* gemm2_weights_scale,
+                   int32_t num_tokens, int32_t num_local_experts, int32_t local_expert_offset,
+                   float routed_scaling_factor, void* output,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Routing only.  topk_idx int32 [T, 8] receives the selected global expert ids
+ * in descending biased-score order (ties: lowest expert id first); topk_weight
+ * f32 [T, 8] the matching normalised, scaled weights.
+ */
+int kf_moe_route(const float* routing_logits, const void* routing_bias, int32_t num_tokens,
+                 float routed_scaling_factor, int32_t* topk_idx, float* topk_weight, void* stream);
+
+/*
+ * Experts only, on pre-routed rows (the expert-parallel receive side).
+ * topk_idx int32 [T, 8] holds global expert ids or -1 (no expert); entries
+ * outside the local range are skipped.  A row's ids must be distinct.
+ * output: bf16 [T, 7168] when output_fp32 == 0, else f32 [T, 7168].
+ */
+int kf_moe_experts(const int32_t* topk_idx, const float* topk_weight,
+                   const void* hidden_states, const float* hidden_states_scale,
+                   const void* gemm1_weights, const float* gemm1_weights_scale,
+                   const void* gemm2_weights, const float* gemm2_weights_scale,
+                   int32_t num_tokens, int32_t num_local_experts, int32_t local_expert_offset,
+                   void* output, int32_t output_fp32,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Synchronises `stream`, then copies the device status word of the last call
+ * that used `workspace` into *status (host pointer) and clears it.  Returns
+ * KF_ERR_DEVICE_STATUS if any bit was set.
+ */
+int kf_moe_read_status(void* workspace, int32_t* status, void* stream);
+
+/* Kernel ids for the profiling counters. */
+#define KF_KERNEL_ROUTE 0
+#define KF_KERNEL_MASKS 1
+#define KF_KERNEL_PERMUTE_SCAN 2
+#define KF_KERNEL_PERMUTE_GATHER 3
+#define KF_KERNEL_GEMM1 4
+#define KF_KERNEL_GEMM2 5
+#define KF_KERNEL_REDUCE 6
+#define KF_KERNEL_COUNT 7
+
+/*
+ * Profiling.  Between kf_moe_profile_begin() and kf_moe_profile_end(), every
+ * kernel this library launches is bracketed by CUDA events recorded on the
+ * launch stream.  kf_moe_profile_end() synchronises those events and writes,
+ * for each kernel id < n, the summed device milliseconds and the launch count.
+ * Host-side bookkeeping only; intended for benchmarks, not for production calls.
+ */
+int kf_moe_profile_begin(void);
+int kf_moe_profile_end(float* total_ms, int32_t* launches, int32_t n);
+
+/* Diagnostics: number of kernels one kf_moe_forward launches. */
+int32_t kf_moe_launches_per_forward(void);
+
+/* Human-readable text for a KF_ERR_* code. */
+const char* kf_moe_error_string(int code);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KF_MOE_H_ */

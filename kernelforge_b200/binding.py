@@ -1,0 +1,244 @@
+"""Python mirror of the reference operator ``kernel(...)`` over the C ABI of ``libkf_moe.so``.
+
+``kernel`` keeps the reference's signature, argument meaning and value-returning
+style (``solution/triton/kernel.py:1817-1828``): ten positional arguments, the
+two scalars given as Python numbers or 0-d tensors, a new bf16 ``[T, 7168]``
+tensor returned on the input device.  Errors raise ``RuntimeError``.
+
+PyTorch is only plumbing here: it owns device memory (outputs and the cached
+workspace come from its caching allocator) and the current stream.  All compute
+runs in the CUDA kernels of ``libkf_moe.so``; there is no CPU or PyTorch
+fallback -- without the library or a B200 the call fails.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from typing import Optional
+
+import torch
+
+H = 7168
+I = 2048
+E_GLOBAL = 256
+TOP_K = 8
+
+_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libkf_moe.so")
+_lib = None
+_lib_lock = threading.Lock()
+
+KF_OK = 0
+KF_ERR_DEVICE_STATUS = 6
+
+
+def _load():
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lib_lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(_LIB_PATH):
+            from . import build as _build
+            _build.build()
+        lib = ctypes.CDLL(_LIB_PATH)
+        vp, i32, f32, sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_float, ctypes.c_size_t
+        lib.kf_moe_workspace_bytes.restype = sz
+        lib.kf_moe_workspace_bytes.argtypes = [i32, i32]
+        lib.kf_moe_forward.restype = ctypes.c_int
+        lib.kf_moe_forward.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, f32, vp, vp, sz, vp]
+        lib.kf_moe_route.restype = ctypes.c_int
+        lib.kf_moe_route.argtypes = [vp, vp, i32, f32, vp, vp, vp]
+        lib.kf_moe_experts.restype = ctypes.c_int
+        lib.kf_moe_experts.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, vp, i32, vp, sz, vp]
+        lib.kf_moe_read_status.restype = ctypes.c_int
+        lib.kf_moe_read_status.argtypes = [vp, ctypes.POINTER(i32), vp]
+        lib.kf_moe_error_string.restype = ctypes.c_char_p
+        lib.kf_moe_error_string.argtypes = [ctypes.c_int]
+        lib.kf_moe_launches_per_forward.restype = i32
+        lib.kf_moe_launches_per_forward.argtypes = []
+        lib.kf_moe_profile_begin.restype = ctypes.c_int
+        lib.kf_moe_profile_begin.argtypes = []
+        lib.kf_moe_profile_end.restype = ctypes.c_int
+        lib.kf_moe_profile_end.argtypes = [ctypes.POINTER(f32), ctypes.POINTER(i32), i32]
+        _lib = lib
+    return _lib
+
+
+def library():
+    """The loaded ``ctypes.CDLL`` (loads it on first use)."""
+    return _load()
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != KF_OK:
+        msg = _load().kf_moe_error_string(rc).decode()
+        raise RuntimeError(f"{what} failed: {msg} (code {rc})")
+
+
+# One workspace per (device, stream): calls queued on one stream run in order, so
+# they can share scratch memory; calls on different streams get their own.
+_workspaces: dict = {}
+_ws_lock = threading.Lock()
+
+
+def workspace(num_tokens: int, num_local: int, device: torch.device, stream: Optional[torch.cuda.Stream] = None):
+    need = int(_load().kf_moe_workspace_bytes(int(num_tokens), int(num_local)))
+    stream = stream or torch.cuda.current_stream(device)
+    key = (device.index, stream.cuda_stream)
+    with _ws_lock:
+        buf = _workspaces.get(key)
+        if buf is None or buf.numel() < need:
+            buf = torch.empty(need, dtype=torch.uint8, device=device)
+            _workspaces[key] = buf
+    return buf
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def _scalar_int(v) -> int:
+    return int(v.item()) if isinstance(v, torch.Tensor) else int(v)
+
+
+def _scalar_float(v) -> float:
+    return float(v.item()) if isinstance(v, torch.Tensor) else float(v)
+
+
+def _expect(t: torch.Tensor, name: str, dtype, shape, device):
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{name} must have shape {tuple(shape)}, got {tuple(t.shape)}")
+    if t.device != device:
+        raise ValueError(f"{name} is on {t.device}, expected {device}")
+    return t.contiguous()
+
+
+def _weights(gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, device):
+    if gemm1_weights.dim() != 3:
+        raise ValueError("gemm1_weights must be [E, 4096, 7168]")
+    E = int(gemm1_weights.shape[0])
+    w13 = _expect(gemm1_weights, "gemm1_weights", torch.float8_e4m3fn, (E, 2 * I, H), device)
+    w13s = _expect(gemm1_weights_scale, "gemm1_weights_scale", torch.float32, (E, 2 * I // 128, H // 128), device)
+    w2 = _expect(gemm2_weights, "gemm2_weights", torch.float8_e4m3fn, (E, H, I), device)
+    w2s = _expect(gemm2_weights_scale, "gemm2_weights_scale", torch.float32, (E, H // 128, I // 128), device)
+    return E, w13, w13s, w2, w2s
+
+
+def kernel(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+           gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
+           routed_scaling_factor):
+    """Fused DeepSeek-V3 FP8 block-scale MoE layer; returns bf16 ``[T, 7168]``.
+
+    Same contract as the reference ``kernel`` (``solution/triton/kernel.py:1817``):
+    routing_logits f32 [T,256], routing_bias bf16 [256], hidden_states e4m3
+    [T,7168], hidden_states_scale f32 [56,T], gemm1_weights e4m3 [E,4096,7168],
+    gemm1_weights_scale f32 [E,32,56], gemm2_weights e4m3 [E,7168,2048],
+    gemm2_weights_scale f32 [E,56,16]; local_expert_offset / routed_scaling_factor
+    as numbers or 0-d tensors.  E (local experts) is taken from the weights.
+    """
+    device = hidden_states.device
+    if device.type != "cuda":
+        raise RuntimeError("kernelforge_b200.kernel needs CUDA tensors on a B200 (sm_100a); no CPU fallback")
+    T = int(routing_logits.shape[0])
+    offset = _scalar_int(local_expert_offset)
+    rsf = _scalar_float(routed_scaling_factor)
+    logits = _expect(routing_logits, "routing_logits", torch.float32, (T, E_GLOBAL), device)
+    bias = _expect(routing_bias.reshape(-1), "routing_bias", torch.bfloat16, (E_GLOBAL,), device)
+    hid = _expect(hidden_states, "hidden_states", torch.float8_e4m3fn, (T, H), device)
+    hs = _expect(hidden_states_scale, "hidden_states_scale", torch.float32, (H // 128, T), device)
+    E, w13, w13s, w2, w2s = _weights(gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, device)
+    if not (0 <= offset and offset + E <= E_GLOBAL):
+        raise ValueError(f"local experts [{offset}, {offset + E}) outside [0, {E_GLOBAL})")
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=device)
+    if T == 0:
+        return out
+    stream = torch.cuda.current_stream(device)
+    ws = workspace(T, E, device, stream)
+    rc = _load().kf_moe_forward(_ptr(logits), _ptr(bias), _ptr(hid), _ptr(hs), _ptr(w13), _ptr(w13s), _ptr(w2),
+                                _ptr(w2s), T, E, offset, ctypes.c_float(rsf), _ptr(out), _ptr(ws),
+                                ctypes.c_size_t(ws.numel()), ctypes.c_void_p(stream.cuda_stream))
+    _check(rc, "kf_moe_forward")
+    return out
+
+
+def route(routing_logits, routing_bias, routed_scaling_factor):
+    """Routing only: ``(topk_idx int32 [T,8], topk_weight f32 [T,8])``, descending score order."""
+    device = routing_logits.device
+    T = int(routing_logits.shape[0])
+    logits = _expect(routing_logits, "routing_logits", torch.float32, (T, E_GLOBAL), device)
+    bias = _expect(routing_bias.reshape(-1), "routing_bias", torch.bfloat16, (E_GLOBAL,), device)
+    idx = torch.empty((T, TOP_K), dtype=torch.int32, device=device)
+    w = torch.empty((T, TOP_K), dtype=torch.float32, device=device)
+    if T:
+        stream = torch.cuda.current_stream(device)
+        rc = _load().kf_moe_route(_ptr(logits), _ptr(bias), T, ctypes.c_float(_scalar_float(routed_scaling_factor)),
+                                  _ptr(idx), _ptr(w), ctypes.c_void_p(stream.cuda_stream))
+        _check(rc, "kf_moe_route")
+    return idx, w
+
+
+def experts(topk_idx, topk_weight, hidden_states, hidden_states_scale, gemm1_weights, gemm1_weights_scale,
+            gemm2_weights, gemm2_weights_scale, local_expert_offset, out_dtype=torch.bfloat16):
+    """Experts on pre-routed rows: ``out[t] = sum_k w[t,k] * FFN_{e[t,k]}(x[t])`` over local experts.
+
+    ``topk_idx`` int32 [T,8] holds global expert ids or -1; ids outside the local
+    range contribute nothing.  Returns ``out_dtype`` (bf16 or f32) ``[T, 7168]``.
+    """
+    device = hidden_states.device
+    T = int(hidden_states.shape[0])
+    idx = _expect(topk_idx, "topk_idx", torch.int32, (T, TOP_K), device)
+    w = _expect(topk_weight, "topk_weight", torch.float32, (T, TOP_K), device)
+    hid = _expect(hidden_states, "hidden_states", torch.float8_e4m3fn, (T, H), device)
+    hs = _expect(hidden_states_scale, "hidden_states_scale", torch.float32, (H // 128, T), device)
+    E, w13, w13s, w2, w2s = _weights(gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, device)
+    offset = _scalar_int(local_expert_offset)
+    if out_dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError("out_dtype must be bfloat16 or float32")
+    out = torch.empty((T, H), dtype=out_dtype, device=device)
+    if T == 0:
+        return out
+    stream = torch.cuda.current_stream(device)
+    ws = workspace(T, E, device, stream)
+    rc = _load().kf_moe_experts(_ptr(idx), _ptr(w), _ptr(hid), _ptr(hs), _ptr(w13), _ptr(w13s), _ptr(w2), _ptr(w2s),
+                                T, E, offset, _ptr(out), 1 if out_dtype == torch.float32 else 0, _ptr(ws),
+                                ctypes.c_size_t(ws.numel()), ctypes.c_void_p(stream.cuda_stream))
+    _check(rc, "kf_moe_experts")
+    return out
+
+
+def read_status(device: Optional[torch.device] = None) -> int:
+    """Synchronise and return (then clear) the device status word of the current stream's workspace."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    stream = torch.cuda.current_stream(device)
+    buf = _workspaces.get((device.index, stream.cuda_stream))
+    if buf is None:
+        return 0
+    st = ctypes.c_int32(0)
+    rc = _load().kf_moe_read_status(_ptr(buf), ctypes.byref(st), ctypes.c_void_p(stream.cuda_stream))
+    if rc not in (KF_OK, KF_ERR_DEVICE_STATUS):
+        _check(rc, "kf_moe_read_status")
+    return int(st.value)
+
+
+KERNEL_NAMES = ["route", "masks_from_topk", "permute_scan", "permute_gather", "gemm1_swiglu", "gemm2_weighted",
+                "reduce"]
+
+
+def profile_begin() -> None:
+    """Start bracketing every library kernel launch with CUDA events."""
+    _check(_load().kf_moe_profile_begin(), "kf_moe_profile_begin")
+
+
+def profile_end() -> dict:
+    """Stop profiling; returns ``{kernel: (total_ms, launches)}`` (synchronises the events)."""
+    n = len(KERNEL_NAMES)
+    ms = (ctypes.c_float * n)()
+    cnt = (ctypes.c_int32 * n)()
+    _check(_load().kf_moe_profile_end(ms, cnt, n), "kf_moe_profile_end")
+    return {KERNEL_NAMES[i]: (float(ms[i]), int(cnt[i])) for i in range(n)}

@@ -1,0 +1,99 @@
+// Internal layout shared by the kernels and the C-ABI layer.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "kf_moe.h"
+
+namespace kf {
+
+constexpr int kH = KF_MOE_HIDDEN;             // 7168
+constexpr int kI = KF_MOE_INTERMEDIATE;       // 2048
+constexpr int kEG = KF_MOE_GLOBAL_EXPERTS;    // 256
+constexpr int kTopK = KF_MOE_TOP_K;           // 8
+constexpr int kBlk = KF_MOE_BLOCK;            // 128 (quantisation block, MMA tile M and K chunk)
+constexpr int kHB = kH / kBlk;                // 56 K-blocks of the hidden dimension
+constexpr int kIB = kI / kBlk;                // 16 K-blocks of the intermediate dimension
+constexpr int kChunkTokens = 128;             // tokens per routing/permute chunk (4 x 32-bit masks)
+constexpr int kMaxLocalExperts = 256;
+
+// Per-call metadata written by the permute scan, read by the GEMMs and the reduce.
+struct Meta {
+  int32_t num_tiles;       // row tiles of 128 permuted rows, over all local experts
+  int32_t num_pairs;       // local (token, expert) pairs
+  int32_t reserved[62];
+  int32_t expert_count[kMaxLocalExperts];      // pairs per local expert
+  int32_t expert_pad_start[kMaxLocalExperts];  // first permuted row of each expert (128-aligned)
+};
+
+// Offsets (bytes) of every scratch array inside the caller's workspace.
+struct Workspace {
+  size_t status, meta, topk_idx, topk_w, token_slot, chunk_masks, chunk_base;
+  size_t tile_expert, tile_row0, tile_rows, slot_token, slot_weight;
+  size_t a_rows, a_scale, c_hi, c_lo, c_scale, y;
+  size_t total;
+  int32_t p_cap;    // capacity in permuted rows (multiple of 128)
+  int32_t nt_cap;   // capacity in row tiles
+  int32_t nchunk;   // routing/permute chunks of 128 tokens
+};
+
+Workspace plan_workspace(int32_t T, int32_t E);
+
+template <typename T>
+inline T* ws_ptr(void* base, size_t off) {
+  return reinterpret_cast<T*>(static_cast<char*>(base) + off);
+}
+
+// Kernel launchers (return cudaGetLastError()).
+cudaError_t launch_route(const float* logits, const void* bias, int T, float rsf, int32_t* topk_idx,
+                         float* topk_w, int E, int offset, uint4* chunk_masks, cudaStream_t s);
+cudaError_t launch_masks_from_topk(const int32_t* topk_idx, int T, int E, int offset, uint4* chunk_masks,
+                                   int* status, cudaStream_t s);
+cudaError_t launch_permute_scan(const uint4* chunk_masks, int nchunk, int E, Meta* meta, int32_t* chunk_base,
+                                int32_t* tile_expert, int32_t* tile_row0, int32_t* tile_rows, int nt_cap,
+                                int* status, cudaStream_t s);
+cudaError_t launch_permute_gather(const int32_t* topk_idx, const float* topk_w, const uint4* chunk_masks,
+                                  const int32_t* chunk_base, const Meta* meta, const uint8_t* hidden,
+                                  const float* hidden_scale, int T, int E, int offset, int p_cap,
+                                  int32_t* token_slot, int32_t* slot_token, float* slot_weight,
+                                  uint8_t* a_rows, float* a_scale, int* status, cudaStream_t s);
+cudaError_t launch_reduce(const int32_t* token_slot, const float* y, int T, void* out, int out_fp32,
+                          cudaStream_t s);
+
+struct Gemm1Args {
+  const Meta* meta;
+  const int32_t* tile_expert;
+  const int32_t* tile_row0;
+  const int32_t* tile_rows;
+  const float* a_scale;    // [56][p_cap]
+  const float* w13_scale;  // [E][32][56]
+  uint8_t* c_hi;           // [p_cap][2048] e4m3
+  uint8_t* c_lo;           // [p_cap][2048] e4m3
+  float* c_scale;          // [16][p_cap]
+  int32_t p_cap;
+  int* status;
+};
+
+struct Gemm2Args {
+  const Meta* meta;
+  const int32_t* tile_expert;
+  const int32_t* tile_row0;
+  const int32_t* tile_rows;
+  const float* c_scale;     // [16][p_cap]
+  const float* w2_scale;    // [E][56][16]
+  const float* slot_weight; // [p_cap]
+  float* y;                 // [p_cap][7168]
+  int32_t p_cap;
+  int* status;
+};
+
+cudaError_t launch_gemm1(const CUtensorMap& tm_a, const CUtensorMap& tm_w13, const Gemm1Args& args, int grid,
+                         cudaStream_t s);
+cudaError_t launch_gemm2(const CUtensorMap& tm_chi, const CUtensorMap& tm_clo, const CUtensorMap& tm_w2,
+                         const Gemm2Args& args, int grid, cudaStream_t s);
+cudaError_t gemm_set_attributes();
+
+}  // namespace kf

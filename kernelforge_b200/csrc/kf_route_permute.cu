@@ -1,0 +1,419 @@
+// Routing, permutation and reduction kernels of the fused MoE layer.
+//
+//   route_kernel          DeepSeek-V3 grouped sigmoid routing, one warp per token
+//                         (reference: solution/triton/kernel.py:1842-1867)
+//   permute_scan_kernel   per-expert counts, 128-aligned segment starts and the
+//                         row-tile work list (reference: _sort_tokens :46-82 and
+//                         the tile metadata of _build_launch_tile_metadata :153-201)
+//   permute_gather_kernel stable slot assignment + gather of FP8 rows and scales
+//   reduce_kernel         atomic-free unpermute-reduce into the output
+//                         (reference: the index_add_ combine :1920-1925)
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "kf_internal.cuh"
+#include "kf_ptx.cuh"
+
+namespace kf {
+
+namespace {
+
+constexpr int kRouteThreads = 256;  // 8 warps, 16 tokens each per chunk
+
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
+  return v > bv || (v == bv && i < bi);
+}
+
+// One warp routes one token.  Lane l owns experts [8l, 8l+8); group g = lanes [4g, 4g+4).
+__global__ void __launch_bounds__(kRouteThreads) route_kernel(const float* __restrict__ logits,
+                                                              const __nv_bfloat16* __restrict__ bias, int T,
+                                                              float rsf, int32_t* __restrict__ topk_idx,
+                                                              float* __restrict__ topk_w, int E, int offset,
+                                                              uint4* __restrict__ chunk_masks) {
+  __shared__ uint32_t masks[kMaxLocalExperts * 4];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int chunk = blockIdx.x;
+  if (chunk_masks) {
+    for (int i = threadIdx.x; i < E * 4; i += blockDim.x) masks[i] = 0u;
+    __syncthreads();
+  }
+  float b[8];
+  {
+    const uint4 raw = *reinterpret_cast<const uint4*>(bias + lane * 8);
+    const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(p[j]);
+      b[2 * j] = f.x;
+      b[2 * j + 1] = f.y;
+    }
+  }
+  for (int tl = warp; tl < kChunkTokens; tl += kRouteThreads / 32) {
+    const int t = chunk * kChunkTokens + tl;
+    if (t >= T) break;
+    const float4* lp = reinterpret_cast<const float4*>(logits + static_cast<size_t>(t) * kEG + lane * 8);
+    const float4 x0 = lp[0], x1 = lp[1];
+    const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+    float s[8], sb[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      s[j] = 1.0f / (1.0f + expf(-x[j]));
+      sb[j] = s[j] + b[j];
+    }
+    // group score: sum of the two largest biased scores of the group's 32 experts
+    float m1 = -INFINITY, m2 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (sb[j] > m1) {
+        m2 = m1;
+        m1 = sb[j];
+      } else if (sb[j] > m2) {
+        m2 = sb[j];
+      }
+    }
+#pragma unroll
+    for (int off = 1; off <= 2; off <<= 1) {
+      const float o1 = __shfl_xor_sync(0xffffffffu, m1, off);
+      const float o2 = __shfl_xor_sync(0xffffffffu, m2, off);
+      const float n2 = fmaxf(fminf(m1, o1), fmaxf(m2, o2));
+      m1 = fmaxf(m1, o1);
+      m2 = n2;
+    }
+    const float gscore = m1 + m2;
+    float gs[8];
+#pragma unroll
+    for (int g = 0; g < 8; ++g) gs[g] = __shfl_sync(0xffffffffu, gscore, 4 * g);
+    // keep the 4 best groups (ties: lower group index wins)
+    const int my_group = lane >> 2;
+    int rank = 0;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) rank += better(gs[g], g, gs[my_group], my_group) ? 1 : 0;
+    uint32_t avail = (rank < 4) ? 0xFFu : 0u;
+    // top-8 over the kept experts by biased score (ties: lower expert id wins)
+    int sel[8];
+    float sel_s[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if ((avail >> j) & 1u) {
+          if (better(sb[j], lane * 8 + j, bv, bi)) {
+            bv = sb[j];
+            bi = lane * 8 + j;
+          }
+        }
+      }
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (better(ov, oi, bv, bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      sel[k] = bi;
+      const int owner = bi >> 3, jj = bi & 7;
+      float mine = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j == jj) mine = s[j];
+      sel_s[k] = __shfl_sync(0xffffffffu, mine, owner);
+      if (lane == owner) avail &= ~(1u << jj);
+    }
+    // normalise the un-biased scores in ascending expert order, then scale
+    float sum = 0.f;
+    {
+      int order[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        int r = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) r += (sel[q] < sel[k]) ? 1 : 0;
+        order[k] = r;
+      }
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        float v = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (order[k] == r) v = sel_s[k];
+        sum += v;
+      }
+    }
+    const float denom = sum + 1e-20f;
+    if (lane < 8) {
+      int e = 0;
+      float w = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (k == lane) {
+          e = sel[k];
+          w = (sel_s[k] / denom) * rsf;
+        }
+      topk_idx[static_cast<size_t>(t) * kTopK + lane] = e;
+      topk_w[static_cast<size_t>(t) * kTopK + lane] = w;
+      if (chunk_masks) {
+        const int le = e - offset;
+        if (le >= 0 && le < E) atomicOr(&masks[le * 4 + (tl >> 5)], 1u << (tl & 31));
+      }
+    }
+  }
+  if (chunk_masks) {
+    __syncthreads();
+    uint4* dst = chunk_masks + static_cast<size_t>(chunk) * E;
+    for (int e = threadIdx.x; e < E; e += blockDim.x)
+      dst[e] = make_uint4(masks[e * 4], masks[e * 4 + 1], masks[e * 4 + 2], masks[e * 4 + 3]);
+  }
+}
+
+// Token bitmasks per local expert from externally supplied routing (expert-parallel receive side).
+__global__ void __launch_bounds__(256) masks_from_topk_kernel(const int32_t* __restrict__ topk_idx, int T, int E,
+                                                              int offset, uint4* __restrict__ chunk_masks,
+                                                              int* status) {
+  __shared__ uint32_t masks[kMaxLocalExperts * 4];
+  const int chunk = blockIdx.x;
+  for (int i = threadIdx.x; i < E * 4; i += blockDim.x) masks[i] = 0u;
+  __syncthreads();
+  for (int p = threadIdx.x; p < kChunkTokens * kTopK; p += blockDim.x) {
+    const int tl = p >> 3;
+    const int t = chunk * kChunkTokens + tl;
+    if (t >= T) break;
+    const int e = topk_idx[static_cast<size_t>(t) * kTopK + (p & 7)];
+    if (e >= kEG) record_error(status, KF_STATUS_BAD_EXPERT);
+    const int le = e - offset;
+    if (e >= 0 && le >= 0 && le < E) atomicOr(&masks[le * 4 + (tl >> 5)], 1u << (tl & 31));
+  }
+  __syncthreads();
+  uint4* dst = chunk_masks + static_cast<size_t>(chunk) * E;
+  for (int e = threadIdx.x; e < E; e += blockDim.x)
+    dst[e] = make_uint4(masks[e * 4], masks[e * 4 + 1], masks[e * 4 + 2], masks[e * 4 + 3]);
+}
+
+__device__ __forceinline__ int popc4(uint4 m) { return __popc(m.x) + __popc(m.y) + __popc(m.z) + __popc(m.w); }
+
+// One block; thread e owns local expert e.  Running counts over chunks give each
+// chunk's base inside the expert's segment (stable: chunk order = token order).
+__global__ void __launch_bounds__(kMaxLocalExperts) permute_scan_kernel(
+    const uint4* __restrict__ chunk_masks, int nchunk, int E, Meta* __restrict__ meta,
+    int32_t* __restrict__ chunk_base, int32_t* __restrict__ tile_expert, int32_t* __restrict__ tile_row0,
+    int32_t* __restrict__ tile_rows, int nt_cap, int* status) {
+  __shared__ int32_t tiles_scan[kMaxLocalExperts];
+  __shared__ int32_t pairs_scan[kMaxLocalExperts];
+  const int e = threadIdx.x;
+  int run = 0;
+  if (e < E) {
+    int c = 0;
+    for (; c + 4 <= nchunk; c += 4) {
+      const uint4 m0 = chunk_masks[static_cast<size_t>(c) * E + e];
+      const uint4 m1 = chunk_masks[static_cast<size_t>(c + 1) * E + e];
+      const uint4 m2 = chunk_masks[static_cast<size_t>(c + 2) * E + e];
+      const uint4 m3 = chunk_masks[static_cast<size_t>(c + 3) * E + e];
+      chunk_base[static_cast<size_t>(c) * E + e] = run;
+      run += popc4(m0);
+      chunk_base[static_cast<size_t>(c + 1) * E + e] = run;
+      run += popc4(m1);
+      chunk_base[static_cast<size_t>(c + 2) * E + e] = run;
+      run += popc4(m2);
+      chunk_base[static_cast<size_t>(c + 3) * E + e] = run;
+      run += popc4(m3);
+    }
+    for (; c < nchunk; ++c) {
+      chunk_base[static_cast<size_t>(c) * E + e] = run;
+      run += popc4(chunk_masks[static_cast<size_t>(c) * E + e]);
+    }
+  }
+  const int ntiles = (run + kBlk - 1) / kBlk;
+  tiles_scan[e] = ntiles;
+  pairs_scan[e] = run;
+  __syncthreads();
+  // inclusive Hillis-Steele scan over 256 entries
+  for (int off = 1; off < kMaxLocalExperts; off <<= 1) {
+    const int a = (e >= off) ? tiles_scan[e - off] : 0;
+    const int b = (e >= off) ? pairs_scan[e - off] : 0;
+    __syncthreads();
+    tiles_scan[e] += a;
+    pairs_scan[e] += b;
+    __syncthreads();
+  }
+  const int tstart = tiles_scan[e] - ntiles;
+  const int total_tiles = tiles_scan[kMaxLocalExperts - 1];
+  if (e < E) {
+    meta->expert_count[e] = run;
+    meta->expert_pad_start[e] = tstart * kBlk;
+    for (int i = 0; i < ntiles; ++i) {
+      const int ti = tstart + i;
+      if (ti >= nt_cap) {
+        record_error(status, KF_STATUS_SLOT_OVERFLOW);
+        break;
+      }
+      tile_expert[ti] = e;
+      tile_row0[ti] = (tstart + i) * kBlk;
+      tile_rows[ti] = min(kBlk, run - i * kBlk);
+    }
+  }
+  if (e == 0) {
+    meta->num_tiles = min(total_tiles, nt_cap);
+    meta->num_pairs = pairs_scan[kMaxLocalExperts - 1];
+  }
+}
+
+// Per chunk: each local pair gets its permuted row (slot) = expert segment start +
+// pairs of that expert in earlier chunks + earlier tokens of this chunk with the
+// same expert (popcount of the mask below the token).  Then the FP8 row and its
+// 56 scales are gathered into the slot.
+__global__ void __launch_bounds__(256) permute_gather_kernel(
+    const int32_t* __restrict__ topk_idx, const float* __restrict__ topk_w, const uint4* __restrict__ chunk_masks,
+    const int32_t* __restrict__ chunk_base, const Meta* __restrict__ meta, const uint8_t* __restrict__ hidden,
+    const float* __restrict__ hidden_scale, int T, int E, int offset, int p_cap, int32_t* __restrict__ token_slot,
+    int32_t* __restrict__ slot_token, float* __restrict__ slot_weight, uint8_t* __restrict__ a_rows,
+    float* __restrict__ a_scale, int* status) {
+  __shared__ uint4 masks[kMaxLocalExperts];
+  __shared__ int32_t base[kMaxLocalExperts];
+  __shared__ int2 pairs[kChunkTokens * kTopK];
+  __shared__ int npairs;
+  const int chunk = blockIdx.x;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    masks[e] = chunk_masks[static_cast<size_t>(chunk) * E + e];
+    base[e] = meta->expert_pad_start[e] + chunk_base[static_cast<size_t>(chunk) * E + e];
+  }
+  if (threadIdx.x == 0) npairs = 0;
+  __syncthreads();
+  for (int p = threadIdx.x; p < kChunkTokens * kTopK; p += blockDim.x) {
+    const int tl = p >> 3;
+    const int t = chunk * kChunkTokens + tl;
+    if (t >= T) break;
+    const size_t ti = static_cast<size_t>(t) * kTopK + (p & 7);
+    const int e = topk_idx[ti];
+    const int le = e - offset;
+    int slot = -1;
+    if (e >= 0 && le >= 0 && le < E) {
+      const uint4 m = masks[le];
+      const int w = tl >> 5;
+      const uint32_t below = (1u << (tl & 31)) - 1u;
+      int r = __popc((w == 0 ? m.x : w == 1 ? m.y : w == 2 ? m.z : m.w) & below);
+      if (w > 0) r += __popc(m.x);
+      if (w > 1) r += __popc(m.y);
+      if (w > 2) r += __popc(m.z);
+      slot = base[le] + r;
+      if (slot >= p_cap) {
+        record_error(status, KF_STATUS_SLOT_OVERFLOW);
+        slot = -1;
+      } else {
+        slot_token[slot] = t;
+        slot_weight[slot] = topk_w[ti];
+        const int q = atomicAdd(&npairs, 1);
+        pairs[q] = make_int2(t, slot);
+      }
+    }
+    token_slot[ti] = slot;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n = npairs;
+  for (int i = warp; i < n; i += blockDim.x / 32) {
+    const int2 ts = pairs[i];
+    const uint4* src = reinterpret_cast<const uint4*>(hidden + static_cast<size_t>(ts.x) * kH);
+    uint4* dst = reinterpret_cast<uint4*>(a_rows + static_cast<size_t>(ts.y) * kH);
+#pragma unroll 7
+    for (int j = lane; j < kH / 16; j += 32) dst[j] = src[j];
+    for (int kb = lane; kb < kHB; kb += 32)
+      a_scale[static_cast<size_t>(kb) * p_cap + ts.y] = hidden_scale[static_cast<size_t>(kb) * T + ts.x];
+  }
+}
+
+// out[t] = sum of the token's permuted rows of y (already routing-weighted), in
+// ascending row order (= ascending local expert, the reference's index_add_ order).
+__global__ void __launch_bounds__(256) reduce_kernel(const int32_t* __restrict__ token_slot,
+                                                     const float* __restrict__ y, int T, void* __restrict__ out,
+                                                     int out_fp32) {
+  const int t = blockIdx.x;
+  int sl[8];
+  int n = 0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int v = token_slot[static_cast<size_t>(t) * kTopK + k];
+    sl[k] = v < 0 ? 0x7fffffff : v;
+    n += v >= 0 ? 1 : 0;
+  }
+  // sort ascending (8-element odd-even transposition network)
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+#pragma unroll
+    for (int k = (r & 1); k + 1 < 8; k += 2) {
+      const int a = sl[k], b = sl[k + 1];
+      sl[k] = min(a, b);
+      sl[k + 1] = max(a, b);
+    }
+  }
+  for (int c = threadIdx.x; c < kH / 4; c += blockDim.x) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      if (k < n) {
+        const float4 v = reinterpret_cast<const float4*>(y + static_cast<size_t>(sl[k]) * kH)[c];
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+    }
+    if (out_fp32) {
+      reinterpret_cast<float4*>(static_cast<float*>(out) + static_cast<size_t>(t) * kH)[c] = acc;
+    } else {
+      __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
+      __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
+      uint2 packed;
+      packed.x = *reinterpret_cast<uint32_t*>(&lo);
+      packed.y = *reinterpret_cast<uint32_t*>(&hi);
+      reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(out) + static_cast<size_t>(t) * kH)[c] = packed;
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_route(const float* logits, const void* bias, int T, float rsf, int32_t* topk_idx,
+                         float* topk_w, int E, int offset, uint4* chunk_masks, cudaStream_t s) {
+  const int nchunk = (T + kChunkTokens - 1) / kChunkTokens;
+  route_kernel<<<nchunk, kRouteThreads, 0, s>>>(logits, static_cast<const __nv_bfloat16*>(bias), T, rsf, topk_idx,
+                                                topk_w, E, offset, chunk_masks);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_masks_from_topk(const int32_t* topk_idx, int T, int E, int offset, uint4* chunk_masks,
+                                   int* status, cudaStream_t s) {
+  const int nchunk = (T + kChunkTokens - 1) / kChunkTokens;
+  masks_from_topk_kernel<<<nchunk, 256, 0, s>>>(topk_idx, T, E, offset, chunk_masks, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_permute_scan(const uint4* chunk_masks, int nchunk, int E, Meta* meta, int32_t* chunk_base,
+                                int32_t* tile_expert, int32_t* tile_row0, int32_t* tile_rows, int nt_cap,
+                                int* status, cudaStream_t s) {
+  permute_scan_kernel<<<1, kMaxLocalExperts, 0, s>>>(chunk_masks, nchunk, E, meta, chunk_base, tile_expert,
+                                                     tile_row0, tile_rows, nt_cap, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_permute_gather(const int32_t* topk_idx, const float* topk_w, const uint4* chunk_masks,
+                                  const int32_t* chunk_base, const Meta* meta, const uint8_t* hidden,
+                                  const float* hidden_scale, int T, int E, int offset, int p_cap,
+                                  int32_t* token_slot, int32_t* slot_token, float* slot_weight,
+                                  uint8_t* a_rows, float* a_scale, int* status, cudaStream_t s) {
+  const int nchunk = (T + kChunkTokens - 1) / kChunkTokens;
+  permute_gather_kernel<<<nchunk, 256, 0, s>>>(topk_idx, topk_w, chunk_masks, chunk_base, meta, hidden,
+                                               hidden_scale, T, E, offset, p_cap, token_slot, slot_token,
+                                               slot_weight, a_rows, a_scale, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_reduce(const int32_t* token_slot, const float* y, int T, void* out, int out_fp32,
+                          cudaStream_t s) {
+  reduce_kernel<<<T, 256, 0, s>>>(token_slot, y, T, out, out_fp32);
+  return cudaGetLastError();
+}
+
+}  // namespace kf

@@ -77,13 +77,13 @@ def sort_tokens(topk_idx: torch.Tensor, local_start: int, num_local: int):
     T, K = topk_idx.shape
     local = topk_idx.to(torch.int64) - int(local_start)
     valid = ((local >= 0) & (local < num_local)).reshape(-1)
-    tok = torch.arange(T, dtype=torch.int64).unsqueeze(1).expand(T, K).reshape(-1)[valid]
+    tok = torch.arange(T, dtype=torch.int64, device=topk_idx.device).unsqueeze(1).expand(T, K).reshape(-1)[valid]
     le = local.reshape(-1)[valid]
     order = torch.argsort(le, stable=True)
     sorted_ids = tok[order]
     sorted_le = le[order]
     counts = torch.bincount(sorted_le, minlength=num_local)
-    starts = torch.zeros(num_local, dtype=torch.int64)
+    starts = torch.zeros(num_local, dtype=torch.int64, device=topk_idx.device)
     if num_local > 1:
         starts[1:] = torch.cumsum(counts, 0)[:-1]
     return sorted_ids, sorted_le, starts, counts
@@ -120,6 +120,8 @@ def moe_layer(routing_logits, routing_bias, hidden_states, hidden_states_scale,
 
     Output: bf16 ``[T, 7168]``.  The number of local experts comes from the weight
     shape (the reference fixes it at 32; expert-parallel shards use 32..256).
+    Runs on the inputs' device: on CPU it is the oracle, on a GPU the tests use
+    the same fp32 code as a full-size reference.
     """
     if isinstance(local_expert_offset, torch.Tensor):
         local_expert_offset = int(local_expert_offset.item())
@@ -129,7 +131,7 @@ def moe_layer(routing_logits, routing_bias, hidden_states, hidden_states_scale,
     E = gemm1_weights.shape[0]
     topk_idx, weights = route(routing_logits, routing_bias, routed_scaling_factor)
     sorted_ids, _, starts, counts = sort_tokens(topk_idx, local_expert_offset, E)
-    acc = torch.zeros(T, H, dtype=torch.float32)
+    acc = torch.zeros(T, H, dtype=torch.float32, device=routing_logits.device)
     for e in torch.nonzero(counts > 0).flatten().tolist():
         tok = sorted_ids[int(starts[e]): int(starts[e]) + int(counts[e])]
         rows = dequant_hidden_rows(hidden_states, hidden_states_scale, tok)
@@ -141,6 +143,31 @@ def moe_layer(routing_logits, routing_bias, hidden_states, hidden_states_scale,
     if return_routing:
         return out, topk_idx, weights
     return out
+
+
+def moe_experts(topk_idx, topk_weight, hidden_states, hidden_states_scale, gemm1_weights,
+                gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset):
+    """Experts on pre-routed rows, fp32 ``[T, 7168]`` (the expert-parallel receive side).
+
+    ``topk_idx`` holds global expert ids or -1; ids outside the local range are
+    skipped.  Per expert the math is the reference loop (``kernel.py:1927-1950``)
+    with the routing weight taken from ``topk_weight``; experts are accumulated
+    in ascending order, as ``index_add_`` over the expert-sorted pairs does.
+    """
+    T = hidden_states.shape[0]
+    E = gemm1_weights.shape[0]
+    loc = topk_idx.to(torch.int64) - int(local_expert_offset)
+    valid = (topk_idx >= 0) & (loc >= 0) & (loc < E)
+    acc = torch.zeros(T, H, dtype=torch.float32, device=hidden_states.device)
+    for e in sorted(set(loc[valid].tolist())):
+        m = valid & (loc == e)
+        tok = torch.nonzero(m.any(dim=1)).flatten()
+        rw = (topk_weight.to(torch.float32) * m).sum(dim=1)[tok]
+        rows = dequant_hidden_rows(hidden_states, hidden_states_scale, tok)
+        y = expert_forward(rows, gemm1_weights[e], gemm1_weights_scale[e],
+                           gemm2_weights[e], gemm2_weights_scale[e])
+        acc.index_add_(0, tok, y * rw.unsqueeze(1))
+    return acc
 
 
 def active_local_experts(routing_logits, routing_bias, local_expert_offset: int, num_local: int):

@@ -1,0 +1,83 @@
+"""The C-ABI library: builds, loads and exports every entry point ``include/kf_moe.h`` declares.
+
+No compute calls here (no GPU in the CPU tier): host-only entry points are called,
+device entry points are only resolved.
+"""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from kernelforge_b200 import binding as B
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    text = open(os.path.join(ROOT, "include", "kf_moe.h")).read()
+    return sorted(set(re.findall(r"^\s*(?:[\w\s\*]+?)\b(kf_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_the_entry_points():
+    syms = declared_symbols()
+    for s in ["kf_moe_forward", "kf_moe_route", "kf_moe_experts", "kf_moe_workspace_bytes",
+              "kf_moe_read_status", "kf_moe_error_string", "kf_moe_launches_per_forward"]:
+        assert s in syms
+
+
+def test_library_exports_every_declared_symbol():
+    lib = B.library()
+    for s in declared_symbols():
+        assert hasattr(lib, s), s
+        assert ctypes.cast(getattr(lib, s), ctypes.c_void_p).value
+
+
+def test_workspace_bytes_is_host_only_and_monotone():
+    lib = B.library()
+    a = lib.kf_moe_workspace_bytes(16, 32)
+    b = lib.kf_moe_workspace_bytes(4096, 32)
+    c = lib.kf_moe_workspace_bytes(4096, 256)
+    assert 0 < a < b < c
+    assert lib.kf_moe_workspace_bytes(-1, 32) == 0
+    assert lib.kf_moe_workspace_bytes(16, 0) == 0
+    assert lib.kf_moe_workspace_bytes(16, 257) == 0
+    # worst case: every token on min(8, E) local experts, each expert padded to 128 rows
+    rows = ((4096 * 8 + 32 * 127) + 127) // 128 * 128
+    assert b > rows * (7168 + 2 * 2048 + 7168 * 4)
+
+
+def test_error_strings():
+    lib = B.library()
+    assert lib.kf_moe_error_string(0) == b"ok"
+    assert b"workspace" in lib.kf_moe_error_string(2)
+    assert lib.kf_moe_launches_per_forward() == 6
+
+
+def test_invalid_arguments_rejected_before_any_device_work():
+    lib = B.library()
+    null = ctypes.c_void_p(0)
+    # E out of range / offset out of range / null pointers: rejected on the host
+    rc = lib.kf_moe_forward(null, null, null, null, null, null, null, null, 4, 0, 0, ctypes.c_float(1.0), null,
+                            null, ctypes.c_size_t(0), null)
+    assert rc == 1
+    rc = lib.kf_moe_forward(null, null, null, null, null, null, null, null, 4, 32, 240, ctypes.c_float(1.0), null,
+                            null, ctypes.c_size_t(0), null)
+    assert rc == 1
+    rc = lib.kf_moe_forward(null, null, null, null, null, null, null, null, 4, 32, 0, ctypes.c_float(1.0), null,
+                            null, ctypes.c_size_t(0), null)
+    assert rc == 1
+    # T == 0 is a no-op
+    rc = lib.kf_moe_forward(null, null, null, null, null, null, null, null, 0, 32, 0, ctypes.c_float(1.0), null,
+                            null, ctypes.c_size_t(0), null)
+    assert rc == 0
+
+
+def test_python_kernel_refuses_cpu_tensors():
+    from kernelforge_b200 import synthetic as S
+    ti = S.token_inputs(2, seed=0)
+    wb = S.expert_bank(1, 0, only=[])
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        B.kernel(ti.routing_logits, ti.routing_bias, ti.hidden_states, ti.hidden_states_scale,
+                 wb.gemm1_weights, wb.gemm1_weights_scale, wb.gemm2_weights, wb.gemm2_weights_scale, 0, 2.5)
