@@ -1,0 +1,52 @@
+"""Worker for the multi-GPU expert-parallel test (NCCL, one process per GPU)."""
+import datetime
+import os
+import sys
+import traceback
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+
+def worker(rank, world, port, T, result_dir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    res = {"rank": rank}
+    try:
+        from kernelforge_b200 import binding as B
+        from kernelforge_b200 import ep
+        from kernelforge_b200 import synthetic as S
+        from oracle import moe_oracle as O
+        dev = torch.device("cuda", rank)
+        torch.cuda.set_device(dev)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=dev)
+        E = 256 // world
+        ti = S.token_inputs(T, seed=60 + rank, device=dev)
+        shard = S.expert_bank(E, rank * E, seed=3, device=dev)
+        layer = ep.ExpertParallelMoE(shard, rank * E, E, combine_dtype=torch.float32)
+        out = layer.forward(ti.routing_logits, ti.routing_bias, ti.hidden_states, ti.hidden_states_scale, 2.5)
+        torch.cuda.synchronize(dev)
+        res["status"] = B.read_status(dev)
+        # single-GPU reference on this rank's tokens: all 256 experts resident here
+        full = S.expert_bank(256, 0, seed=3, device=dev)
+        single = B.kernel(ti.routing_logits, ti.routing_bias, ti.hidden_states, ti.hidden_states_scale,
+                          full.gemm1_weights, full.gemm1_weights_scale, full.gemm2_weights,
+                          full.gemm2_weights_scale, 0, 2.5)
+        idx, w = B.route(ti.routing_logits, ti.routing_bias, 2.5)
+        ref = O.moe_experts(idx, w, ti.hidden_states, ti.hidden_states_scale, full.gemm1_weights,
+                            full.gemm1_weights_scale, full.gemm2_weights, full.gemm2_weights_scale, 0)
+        res["ep_vs_ref"] = O.check_tolerance(out, ref.to(torch.bfloat16))
+        res["single_vs_ref"] = O.check_tolerance(single, ref.to(torch.bfloat16))
+        res["ep_vs_single_maxdiff"] = float((out.float() - single.float()).abs().max())
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as exc:
+        res["error"] = f"{type(exc).__name__}: {exc}"
+        res["trace"] = traceback.format_exc()
+    torch.save(res, os.path.join(result_dir, f"g{rank}.pt"))
