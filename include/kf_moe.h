@@ -50,6 +50,7 @@ extern "C" {
 #define KF_ERR_UNSUPPORTED_DEVICE 4
 #define KF_ERR_DRIVER_ENTRY_POINT 5
 #define KF_ERR_DEVICE_STATUS 6
+#define KF_ERR_EXCEEDS_STATIC_SCRATCH 7
 
 /* Device status bits (OR-ed into the workspace status word by the kernels). */
 #define KF_STATUS_TIMEOUT_PRODUCER 0x01 /* a TMA producer waited too long for a free stage */
@@ -117,6 +118,45 @@ int kf_moe_experts(const int32_t* topk_idx, const float* topk_weight,
  * KF_ERR_DEVICE_STATUS if any bit was set.
  */
 int kf_moe_read_status(void* workspace, int32_t* status, void* stream);
+
+/* Limits of kf_moe_forward_noalloc and the size of its static scratch array. */
+#define KF_MOE_NOALLOC_MAX_TOKENS 16
+#define KF_MOE_NOALLOC_MAX_LOCAL_EXPERTS 32
+#define KF_MOE_NOALLOC_SCRATCH_BYTES (163u << 20) /* 163 MiB */
+
+/*
+ * kf_moe_forward for callers that cannot allocate device memory.  This entry
+ * point has no counterpart in the reference (its kernel() allocates through
+ * torch on every call).
+ *
+ * Some callers cannot call cudaMalloc, so they cannot hand kf_moe_forward a
+ * workspace: a plugin host that owns all device memory and passes a plugin only
+ * its input and output buffers, a host language bound to this C ABI without any
+ * CUDA allocation binding, or a serving process whose device memory is already
+ * fully reserved by its own pools.  This variant takes the same inputs and
+ * output but no workspace: its scratch memory is a file-scope static device
+ * array of KF_MOE_NOALLOC_SCRATCH_BYTES, which every GPU that loads this library
+ * holds until the process exits.  It calls no cudaMalloc, cudaFree or other
+ * allocating routine.
+ *
+ * Limits: num_tokens <= KF_MOE_NOALLOC_MAX_TOKENS and num_local_experts <=
+ * KF_MOE_NOALLOC_MAX_LOCAL_EXPERTS (decode-sized calls of the e32 layer);
+ * larger calls return KF_ERR_EXCEEDS_STATIC_SCRATCH without doing any work.
+ * The first call on a device looks up that device's copy of the array (with
+ * that device current); make that first call before any stream capture.
+ * All calls on a device share the one array, which keeps the previous call's
+ * contents (each call clears the status word it needs zeroed and overwrites
+ * everything else before reading it): calls that overlap on the GPU -- on
+ * different streams or from different threads -- race on it and must be
+ * serialised by the caller.  Device-side status bits of these calls are not
+ * readable through kf_moe_read_status.
+ */
+int kf_moe_forward_noalloc(const float* routing_logits, const void* routing_bias,
+                           const void* hidden_states, const float* hidden_states_scale,
+                           const void* gemm1_weights, const float* gemm1_weights_scale,
+                           const void* gemm2_weights, const float* gemm2_weights_scale,
+                           int32_t num_tokens, int32_t num_local_experts, int32_t local_expert_offset,
+                           float routed_scaling_factor, void* output, void* stream);
 
 /* Kernel ids for the profiling counters. */
 #define KF_KERNEL_ROUTE 0

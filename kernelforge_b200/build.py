@@ -19,7 +19,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libkf_moe.so")
-SOURCES = ["kf_route_permute.cu", "kf_grouped_gemm.cu", "kf_moe_api.cu"]
+SOURCES = ["kf_route_permute.cu", "kf_grouped_gemm.cu", "kf_moe_api.cu", "kf_moe_noalloc.cu"]
 HEADERS = ["kf_ptx.cuh", "kf_internal.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -254,6 +254,7 @@ const char* kf_moe_error_string(int code) {
     case KF_ERR_UNSUPPORTED_DEVICE: return "unsupported device (needs sm_100a / B200)";
     case KF_ERR_DRIVER_ENTRY_POINT: return "cuTensorMapEncodeTiled unavailable";
     case KF_ERR_DEVICE_STATUS: return "device-side error (see status bits)";
+    case KF_ERR_EXCEEDS_STATIC_SCRATCH: return "call exceeds the static scratch of kf_moe_forward_noalloc";
     default: return "unknown error";
   }
 }
