@@ -162,11 +162,12 @@ int kf_moe_forward_noalloc(const float* routing_logits, const void* routing_bias
 #define KF_KERNEL_ROUTE 0
 #define KF_KERNEL_MASKS 1
 #define KF_KERNEL_PERMUTE_SCAN 2
-#define KF_KERNEL_PERMUTE_GATHER 3
-#define KF_KERNEL_GEMM1 4
-#define KF_KERNEL_GEMM2 5
-#define KF_KERNEL_REDUCE 6
-#define KF_KERNEL_COUNT 7
+#define KF_KERNEL_PERMUTE_ASSIGN 3
+#define KF_KERNEL_GATHER_ROWS 4
+#define KF_KERNEL_GEMM1 5
+#define KF_KERNEL_GEMM2 6
+#define KF_KERNEL_REDUCE 7
+#define KF_KERNEL_COUNT 8
 
 /*
  * Profiling.  Between kf_moe_profile_begin() and kf_moe_profile_end(), every

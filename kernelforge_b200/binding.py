@@ -226,8 +226,8 @@ def read_status(device: Optional[torch.device] = None) -> int:
     return int(st.value)
 
 
-KERNEL_NAMES = ["route", "masks_from_topk", "permute_scan", "permute_gather", "gemm1_swiglu", "gemm2_weighted",
-                "reduce"]
+KERNEL_NAMES = ["route", "masks_from_topk", "permute_scan", "permute_assign", "gather_rows", "gemm1_swiglu",
+                "gemm2_weighted", "unpermute_reduce"]
 
 
 def profile_begin() -> None:

@@ -55,11 +55,13 @@ cudaError_t launch_masks_from_topk(const int32_t* topk_idx, int T, int E, int of
 cudaError_t launch_permute_scan(const uint4* chunk_masks, int nchunk, int E, Meta* meta, int32_t* chunk_base,
                                 int32_t* tile_expert, int32_t* tile_row0, int32_t* tile_rows, int nt_cap,
                                 int* status, cudaStream_t s);
-cudaError_t launch_permute_gather(const int32_t* topk_idx, const float* topk_w, const uint4* chunk_masks,
-                                  const int32_t* chunk_base, const Meta* meta, const uint8_t* hidden,
-                                  const float* hidden_scale, int T, int E, int offset, int p_cap,
-                                  int32_t* token_slot, int32_t* slot_token, float* slot_weight,
-                                  uint8_t* a_rows, float* a_scale, int* status, cudaStream_t s);
+cudaError_t launch_permute_assign(const int32_t* topk_idx, const float* topk_w, const uint4* chunk_masks,
+                                  const int32_t* chunk_base, const Meta* meta, int T, int E, int offset, int p_cap,
+                                  int32_t* token_slot, int32_t* slot_token, float* slot_weight, int* status,
+                                  cudaStream_t s);
+cudaError_t launch_gather_rows(const Meta* meta, const int32_t* tile_rows, const int32_t* slot_token,
+                               const uint8_t* hidden, const float* hidden_scale, int T, int p_cap, uint8_t* a_rows,
+                               float* a_scale, int grid, cudaStream_t s);
 cudaError_t launch_reduce(const int32_t* token_slot, const float* y, int T, void* out, int out_fp32,
                           cudaStream_t s);
 

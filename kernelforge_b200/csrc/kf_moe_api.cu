@@ -124,20 +124,27 @@ int run_experts(const Workspace& w, void* ws, const int32_t* topk_idx, const flo
   int* status = ws_ptr<int>(ws, w.status);
   Meta* meta = ws_ptr<Meta>(ws, w.meta);
   {
-  ProfScope ps(KF_KERNEL_PERMUTE_SCAN, s);
-  if (launch_permute_scan(ws_ptr<uint4>(ws, w.chunk_masks), w.nchunk, E, meta, ws_ptr<int32_t>(ws, w.chunk_base),
-                          ws_ptr<int32_t>(ws, w.tile_expert), ws_ptr<int32_t>(ws, w.tile_row0),
-                          ws_ptr<int32_t>(ws, w.tile_rows), w.nt_cap, status, s) != cudaSuccess)
-    return KF_ERR_CUDA;
+    ProfScope ps(KF_KERNEL_PERMUTE_SCAN, s);
+    if (launch_permute_scan(ws_ptr<uint4>(ws, w.chunk_masks), w.nchunk, E, meta, ws_ptr<int32_t>(ws, w.chunk_base),
+                            ws_ptr<int32_t>(ws, w.tile_expert), ws_ptr<int32_t>(ws, w.tile_row0),
+                            ws_ptr<int32_t>(ws, w.tile_rows), w.nt_cap, status, s) != cudaSuccess)
+      return KF_ERR_CUDA;
   }
   {
-  ProfScope ps(KF_KERNEL_PERMUTE_GATHER, s);
-  if (launch_permute_gather(topk_idx, topk_w, ws_ptr<uint4>(ws, w.chunk_masks), ws_ptr<int32_t>(ws, w.chunk_base),
-                            meta, static_cast<const uint8_t*>(hidden), hidden_scale, T, E, offset, w.p_cap,
-                            ws_ptr<int32_t>(ws, w.token_slot), ws_ptr<int32_t>(ws, w.slot_token),
-                            ws_ptr<float>(ws, w.slot_weight), ws_ptr<uint8_t>(ws, w.a_rows),
-                            ws_ptr<float>(ws, w.a_scale), status, s) != cudaSuccess)
-    return KF_ERR_CUDA;
+    ProfScope ps(KF_KERNEL_PERMUTE_ASSIGN, s);
+    if (launch_permute_assign(topk_idx, topk_w, ws_ptr<uint4>(ws, w.chunk_masks), ws_ptr<int32_t>(ws, w.chunk_base),
+                              meta, T, E, offset, w.p_cap, ws_ptr<int32_t>(ws, w.token_slot),
+                              ws_ptr<int32_t>(ws, w.slot_token), ws_ptr<float>(ws, w.slot_weight), status,
+                              s) != cudaSuccess)
+      return KF_ERR_CUDA;
+  }
+  {
+    ProfScope ps(KF_KERNEL_GATHER_ROWS, s);
+    if (launch_gather_rows(meta, ws_ptr<int32_t>(ws, w.tile_rows), ws_ptr<int32_t>(ws, w.slot_token),
+                           static_cast<const uint8_t*>(hidden), hidden_scale, T, w.p_cap,
+                           ws_ptr<uint8_t>(ws, w.a_rows), ws_ptr<float>(ws, w.a_scale), 4 * num_sms,
+                           s) != cudaSuccess)
+      return KF_ERR_CUDA;
   }
 
   CUtensorMap tm_a, tm_w13, tm_chi, tm_clo, tm_w2;
@@ -243,7 +250,7 @@ size_t kf_moe_workspace_bytes(int32_t num_tokens, int32_t num_local_experts) {
   return plan_workspace(num_tokens, num_local_experts).total;
 }
 
-int32_t kf_moe_launches_per_forward(void) { return 6; }
+int32_t kf_moe_launches_per_forward(void) { return 7; }
 
 const char* kf_moe_error_string(int code) {
   switch (code) {

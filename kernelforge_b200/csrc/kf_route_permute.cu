@@ -5,8 +5,9 @@
 //   permute_scan_kernel   per-expert counts, 128-aligned segment starts and the
 //                         row-tile work list (reference: _sort_tokens :46-82 and
 //                         the tile metadata of _build_launch_tile_metadata :153-201)
-//   permute_gather_kernel stable slot assignment + gather of FP8 rows and scales
-//   reduce_kernel         atomic-free unpermute-reduce into the output
+//   permute_assign_kernel stable slot of every local (token, expert) pair
+//   gather_rows_kernel    gather of FP8 rows and scales into expert-contiguous rows
+//   unpermute_reduce_kernel  atomic-free unpermute-reduce into the output
 //                         (reference: the index_add_ combine :1920-1925)
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -18,7 +19,7 @@ namespace kf {
 
 namespace {
 
-constexpr int kRouteThreads = 256;  // 8 warps, 16 tokens each per chunk
+constexpr int kRouteThreads = 1024;  // 32 warps, 4 tokens each per chunk of 128
 
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
   return v > bv || (v == bv && i < bi);
@@ -262,24 +263,21 @@ __global__ void __launch_bounds__(kMaxLocalExperts) permute_scan_kernel(
 
 // Per chunk: each local pair gets its permuted row (slot) = expert segment start +
 // pairs of that expert in earlier chunks + earlier tokens of this chunk with the
-// same expert (popcount of the mask below the token).  Then the FP8 row and its
-// 56 scales are gathered into the slot.
-__global__ void __launch_bounds__(256) permute_gather_kernel(
+// same expert (popcount of the mask below the token).  Stable and deterministic:
+// the order inside an expert's segment is token order, as the reference's
+// stable argsort gives (solution/triton/kernel.py:67-69).
+__global__ void __launch_bounds__(256) permute_assign_kernel(
     const int32_t* __restrict__ topk_idx, const float* __restrict__ topk_w, const uint4* __restrict__ chunk_masks,
-    const int32_t* __restrict__ chunk_base, const Meta* __restrict__ meta, const uint8_t* __restrict__ hidden,
-    const float* __restrict__ hidden_scale, int T, int E, int offset, int p_cap, int32_t* __restrict__ token_slot,
-    int32_t* __restrict__ slot_token, float* __restrict__ slot_weight, uint8_t* __restrict__ a_rows,
-    float* __restrict__ a_scale, int* status) {
+    const int32_t* __restrict__ chunk_base, const Meta* __restrict__ meta, int T, int E, int offset, int p_cap,
+    int32_t* __restrict__ token_slot, int32_t* __restrict__ slot_token, float* __restrict__ slot_weight,
+    int* status) {
   __shared__ uint4 masks[kMaxLocalExperts];
   __shared__ int32_t base[kMaxLocalExperts];
-  __shared__ int2 pairs[kChunkTokens * kTopK];
-  __shared__ int npairs;
   const int chunk = blockIdx.x;
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     masks[e] = chunk_masks[static_cast<size_t>(chunk) * E + e];
     base[e] = meta->expert_pad_start[e] + chunk_base[static_cast<size_t>(chunk) * E + e];
   }
-  if (threadIdx.x == 0) npairs = 0;
   __syncthreads();
   for (int p = threadIdx.x; p < kChunkTokens * kTopK; p += blockDim.x) {
     const int tl = p >> 3;
@@ -304,29 +302,43 @@ __global__ void __launch_bounds__(256) permute_gather_kernel(
       } else {
         slot_token[slot] = t;
         slot_weight[slot] = topk_w[ti];
-        const int q = atomicAdd(&npairs, 1);
-        pairs[q] = make_int2(t, slot);
       }
     }
     token_slot[ti] = slot;
   }
-  __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n = npairs;
-  for (int i = warp; i < n; i += blockDim.x / 32) {
-    const int2 ts = pairs[i];
-    const uint4* src = reinterpret_cast<const uint4*>(hidden + static_cast<size_t>(ts.x) * kH);
-    uint4* dst = reinterpret_cast<uint4*>(a_rows + static_cast<size_t>(ts.y) * kH);
-#pragma unroll 7
-    for (int j = lane; j < kH / 16; j += 32) dst[j] = src[j];
+}
+
+// Copies each permuted row's FP8 hidden row (7168 bytes) and its 56 scales into
+// the expert-contiguous A buffer.  One warp per row, grid-strided over all row
+// tiles so every SM streams; padding rows of a tile are skipped.
+__global__ void __launch_bounds__(256) gather_rows_kernel(const Meta* __restrict__ meta,
+                                                          const int32_t* __restrict__ tile_rows,
+                                                          const int32_t* __restrict__ slot_token,
+                                                          const uint8_t* __restrict__ hidden,
+                                                          const float* __restrict__ hidden_scale, int T, int p_cap,
+                                                          uint8_t* __restrict__ a_rows,
+                                                          float* __restrict__ a_scale) {
+  const int lane = threadIdx.x & 31;
+  const int warps = blockDim.x >> 5;
+  const int nrows = meta->num_tiles * kBlk;
+  for (int r = blockIdx.x * warps + (threadIdx.x >> 5); r < nrows; r += gridDim.x * warps) {
+    if ((r & (kBlk - 1)) >= tile_rows[r >> 7]) continue;
+    const int t = slot_token[r];
+    const uint4* src = reinterpret_cast<const uint4*>(hidden + static_cast<size_t>(t) * kH);
+    uint4* dst = reinterpret_cast<uint4*>(a_rows + static_cast<size_t>(r) * kH);
+    uint4 v[kH / 16 / 32];
+#pragma unroll
+    for (int j = 0; j < kH / 16 / 32; ++j) v[j] = src[lane + 32 * j];
+#pragma unroll
+    for (int j = 0; j < kH / 16 / 32; ++j) dst[lane + 32 * j] = v[j];
     for (int kb = lane; kb < kHB; kb += 32)
-      a_scale[static_cast<size_t>(kb) * p_cap + ts.y] = hidden_scale[static_cast<size_t>(kb) * T + ts.x];
+      a_scale[static_cast<size_t>(kb) * p_cap + r] = hidden_scale[static_cast<size_t>(kb) * T + t];
   }
 }
 
 // out[t] = sum of the token's permuted rows of y (already routing-weighted), in
 // ascending row order (= ascending local expert, the reference's index_add_ order).
-__global__ void __launch_bounds__(256) reduce_kernel(const int32_t* __restrict__ token_slot,
+__global__ void __launch_bounds__(256) unpermute_reduce_kernel(const int32_t* __restrict__ token_slot,
                                                      const float* __restrict__ y, int T, void* __restrict__ out,
                                                      int out_fp32) {
   const int t = blockIdx.x;
@@ -398,21 +410,27 @@ cudaError_t launch_permute_scan(const uint4* chunk_masks, int nchunk, int E, Met
   return cudaGetLastError();
 }
 
-cudaError_t launch_permute_gather(const int32_t* topk_idx, const float* topk_w, const uint4* chunk_masks,
-                                  const int32_t* chunk_base, const Meta* meta, const uint8_t* hidden,
-                                  const float* hidden_scale, int T, int E, int offset, int p_cap,
-                                  int32_t* token_slot, int32_t* slot_token, float* slot_weight,
-                                  uint8_t* a_rows, float* a_scale, int* status, cudaStream_t s) {
+cudaError_t launch_permute_assign(const int32_t* topk_idx, const float* topk_w, const uint4* chunk_masks,
+                                  const int32_t* chunk_base, const Meta* meta, int T, int E, int offset, int p_cap,
+                                  int32_t* token_slot, int32_t* slot_token, float* slot_weight, int* status,
+                                  cudaStream_t s) {
   const int nchunk = (T + kChunkTokens - 1) / kChunkTokens;
-  permute_gather_kernel<<<nchunk, 256, 0, s>>>(topk_idx, topk_w, chunk_masks, chunk_base, meta, hidden,
-                                               hidden_scale, T, E, offset, p_cap, token_slot, slot_token,
-                                               slot_weight, a_rows, a_scale, status);
+  permute_assign_kernel<<<nchunk, 256, 0, s>>>(topk_idx, topk_w, chunk_masks, chunk_base, meta, T, E, offset, p_cap,
+                                               token_slot, slot_token, slot_weight, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gather_rows(const Meta* meta, const int32_t* tile_rows, const int32_t* slot_token,
+                               const uint8_t* hidden, const float* hidden_scale, int T, int p_cap, uint8_t* a_rows,
+                               float* a_scale, int grid, cudaStream_t s) {
+  gather_rows_kernel<<<grid, 256, 0, s>>>(meta, tile_rows, slot_token, hidden, hidden_scale, T, p_cap, a_rows,
+                                          a_scale);
   return cudaGetLastError();
 }
 
 cudaError_t launch_reduce(const int32_t* token_slot, const float* y, int T, void* out, int out_fp32,
                           cudaStream_t s) {
-  reduce_kernel<<<T, 256, 0, s>>>(token_slot, y, T, out, out_fp32);
+  unpermute_reduce_kernel<<<T, 256, 0, s>>>(token_slot, y, T, out, out_fp32);
   return cudaGetLastError();
 }
 

@@ -52,7 +52,7 @@ def test_error_strings():
     lib = B.library()
     assert lib.kf_moe_error_string(0) == b"ok"
     assert b"workspace" in lib.kf_moe_error_string(2)
-    assert lib.kf_moe_launches_per_forward() == 6
+    assert lib.kf_moe_launches_per_forward() == 7
 
 
 def test_invalid_arguments_rejected_before_any_device_work():
