@@ -33,6 +33,8 @@ namespace {
 
 constexpr int kThreads = 384;  // 12 warps
 constexpr int kEpiWarps = 8;
+constexpr int kScaleRing = 8;  // per-chunk scale slots; decoupled from the operand stages
+constexpr int kSmallRows = 32; // tiles with at most this many valid rows load a 32-row A box
 
 // ------------------------------------------------------------------ GEMM1 --
 // X = A[rows, 7168] . W13[e]^T, N-block = 128 up columns + the matching 128 gate
@@ -43,13 +45,12 @@ constexpr int G1_A = kBlk * kBlk;        // 16 KB
 constexpr int G1_B = 2 * kBlk * kBlk;    // 32 KB: up rows then gate rows
 constexpr int G1_OFF_B = G1_S * G1_A;
 constexpr int G1_OFF_AS = G1_OFF_B + G1_S * G1_B;
-constexpr int G1_OFF_WS = G1_OFF_AS + G1_S * kBlk * 4;
-constexpr int G1_OFF_BAR = G1_OFF_WS + G1_S * 8;
-constexpr int G1_NBAR = 2 * G1_S + 6;
+constexpr int G1_OFF_WS = G1_OFF_AS + kScaleRing * kBlk * 4;
+constexpr int G1_OFF_BAR = G1_OFF_WS + kScaleRing * 8;
+constexpr int G1_NBAR = 2 * G1_S + 2 * kScaleRing + 6;
 constexpr int G1_OFF_MISC = G1_OFF_BAR + G1_NBAR * 8;
 constexpr int G1_OFF_XCH = G1_OFF_MISC + 16;
 constexpr int G1_SMEM = G1_OFF_XCH + 2 * 2 * kBlk * 4 + 1024;
-constexpr uint32_t G1_TX = 3 * 16384 + kBlk * 4;
 
 // ------------------------------------------------------------------ GEMM2 --
 // Y = C[rows, 2048] . W2[e]^T with C = s * (C_hi + C_lo), N-block = 256 output
@@ -61,16 +62,16 @@ constexpr int G2_B = 2 * kBlk * kBlk;    // 32 KB: 256 rows of W2
 constexpr int G2_OFF_ALO = G2_S * G2_A;
 constexpr int G2_OFF_B = 2 * G2_S * G2_A;
 constexpr int G2_OFF_AS = G2_OFF_B + G2_S * G2_B;
-constexpr int G2_OFF_WS = G2_OFF_AS + G2_S * kBlk * 4;
-constexpr int G2_OFF_BAR = G2_OFF_WS + G2_S * 8;
-constexpr int G2_NBAR = 2 * G2_S + 4;
+constexpr int G2_OFF_WS = G2_OFF_AS + kScaleRing * kBlk * 4;
+constexpr int G2_OFF_BAR = G2_OFF_WS + kScaleRing * 8;
+constexpr int G2_NBAR = 2 * G2_S + 2 * kScaleRing + 4;
 constexpr int G2_OFF_MISC = G2_OFF_BAR + G2_NBAR * 8;
 constexpr int G2_SMEM = G2_OFF_MISC + 16 + 1024;
-constexpr uint32_t G2_TX = 2 * 16384 + 32768 + kBlk * 4;
 constexpr int kG2NB = kH / 256;  // 28 column blocks of 256
 
 static_assert(G1_SMEM <= 232448, "GEMM1 shared memory");
 static_assert(G2_SMEM <= 232448, "GEMM2 shared memory");
+static_assert(G1_S <= 32 && G2_S <= 32 && kScaleRing <= 32, "ring bitmasks");
 // Register split (setmaxnreg): warpgroup 0 drops to 40, warpgroups 1-2 rise to
 // 232: 128*40 + 256*232 = 64512 = 384 threads * 168, the launch allocation
 // (__launch_bounds__(384, 1); the build checks ptxas reports 168).
@@ -104,9 +105,37 @@ __device__ __forceinline__ uint2 encode_hilo4(float x0, float x1, float x2, floa
   return make_uint2(hi, lo);
 }
 
+// Ring position: index and phase parity, advanced together.
+struct RingPos {
+  int idx = 0;
+  uint32_t ph = 0;
+  template <int N>
+  __device__ __forceinline__ void advance() {
+    if (++idx == N) {
+      idx = 0;
+      ph ^= 1u;
+    }
+  }
+};
+
+// Bitmask record of the last phase armed on each slot of a ring, so the producer
+// can wait for its in-flight copies before the CTA exits.
+struct ArmedSlots {
+  uint32_t armed = 0, par = 0;
+  __device__ __forceinline__ void set(int i, uint32_t ph) {
+    armed |= 1u << i;
+    par = ph ? (par | (1u << i)) : (par & ~(1u << i));
+  }
+  __device__ __forceinline__ void drain(uint64_t* bars, int n, int* status) const {
+    int no_abort = 0;
+    for (int i = 0; i < n; ++i)
+      if ((armed >> i) & 1u) mbar_wait_abort(&bars[i], (par >> i) & 1u, &no_abort, status, KF_STATUS_TIMEOUT_PRODUCER);
+  }
+};
+
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm1_swiglu_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
-                        const Gemm1Args g) {
+    gemm1_swiglu_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_a32,
+                        const __grid_constant__ CUtensorMap tm_w, const Gemm1Args g) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sA = smem;
@@ -115,8 +144,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   float2* ws_ring = reinterpret_cast<float2*>(smem + G1_OFF_WS);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G1_OFF_BAR);
   uint64_t* full = bars;
-  uint64_t* empty = bars + G1_S;
-  uint64_t* pfull = bars + 2 * G1_S;
+  uint64_t* empty = full + G1_S;
+  uint64_t* sfull = empty + G1_S;
+  uint64_t* sempty = sfull + kScaleRing;
+  uint64_t* pfull = sempty + kScaleRing;
   uint64_t* pempty = pfull + 2;
   uint64_t* xbar = pempty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + G1_OFF_MISC);
@@ -130,7 +161,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < G1_S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1 + kEpiWarps);
+      mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < kScaleRing; ++s) {
+      mbar_init(&sfull[s], 1);
+      mbar_init(&sempty[s], kEpiWarps);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&pfull[b], 1);
@@ -142,6 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_a);
+    tma_prefetch_desc(&tm_a32);
     tma_prefetch_desc(&tm_w);
   }
   if (warp == 1) tmem_alloc(tmem_holder, 512);
@@ -154,13 +190,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     setmaxnreg_dec<kRegsLow>();
     if (warp == 0) {
       // ------------------------------------------------------ TMA producer --
-      int stage = 0;
-      uint32_t ph = 0, armed = 0, armed_par = 0;
+      RingPos st, ss;
+      ArmedSlots armed_st, armed_ss;
       bool ok = true;
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
         const int tile = u / kIB, nb = u % kIB;
         const int e = g.tile_expert[tile];
         const int row0 = g.tile_row0[tile];
+        const bool small = g.tile_rows[tile] <= kSmallRows;
+        const uint32_t tx = (small ? kSmallRows * kBlk : G1_A) + G1_B;
         const float* wsu = g.w13_scale + (static_cast<size_t>(e) * 32 + nb) * kHB;
         const float* wsg = g.w13_scale + (static_cast<size_t>(e) * 32 + kIB + nb) * kHB;
         const float su0 = wsu[lane], sg0 = wsg[lane];
@@ -172,17 +210,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float sg = __shfl_sync(0xffffffffu, kb < 32 ? sg0 : sg1, kb & 31);
           int good = 1;
           if (lane == 0) {
-            good = mbar_wait_abort(&empty[stage], ph ^ 1u, abort_flag, g.status, KF_STATUS_TIMEOUT_PRODUCER);
+            good = mbar_wait_abort(&empty[st.idx], st.ph ^ 1u, abort_flag, g.status, KF_STATUS_TIMEOUT_PRODUCER) &&
+                   mbar_wait_abort(&sempty[ss.idx], ss.ph ^ 1u, abort_flag, g.status, KF_STATUS_TIMEOUT_PRODUCER);
             if (good) {
-              ws_ring[stage] = make_float2(su, sg);
-              mbar_arrive_expect_tx(&full[stage], G1_TX);
-              tma_load_2d(sA + stage * G1_A, &tm_a, kb * kBlk, row0, &full[stage]);
-              tma_load_2d(sB + stage * G1_B, &tm_w, kb * kBlk, wrow_up, &full[stage]);
-              tma_load_2d(sB + stage * G1_B + G1_A, &tm_w, kb * kBlk, wrow_up + kI, &full[stage]);
-              bulk_load(as_ring + stage * kBlk, g.a_scale + static_cast<size_t>(kb) * g.p_cap + row0, kBlk * 4,
-                        &full[stage]);
-              armed |= 1u << stage;
-              armed_par = ph ? (armed_par | (1u << stage)) : (armed_par & ~(1u << stage));
+              ws_ring[ss.idx] = make_float2(su, sg);
+              mbar_arrive_expect_tx(&sfull[ss.idx], kBlk * 4);
+              bulk_load(as_ring + ss.idx * kBlk, g.a_scale + static_cast<size_t>(kb) * g.p_cap + row0, kBlk * 4,
+                        &sfull[ss.idx]);
+              armed_ss.set(ss.idx, ss.ph);
+              mbar_arrive_expect_tx(&full[st.idx], tx);
+              tma_load_2d(sA + st.idx * G1_A, small ? &tm_a32 : &tm_a, kb * kBlk, row0, &full[st.idx]);
+              tma_load_2d(sB + st.idx * G1_B, &tm_w, kb * kBlk, wrow_up, &full[st.idx]);
+              tma_load_2d(sB + st.idx * G1_B + G1_A, &tm_w, kb * kBlk, wrow_up + kI, &full[st.idx]);
+              armed_st.set(st.idx, st.ph);
             }
           }
           good = __shfl_sync(0xffffffffu, good, 0);
@@ -190,59 +230,46 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          if (++stage == G1_S) {
-            stage = 0;
-            ph ^= 1u;
-          }
+          st.advance<G1_S>();
+          ss.advance<kScaleRing>();
         }
       }
-      if (lane == 0) {  // let every TMA write that was issued land before the CTA can exit
-        int no_abort = 0;
-        for (int s = 0; s < G1_S; ++s)
-          if ((armed >> s) & 1u)
-            mbar_wait_abort(&full[s], (armed_par >> s) & 1u, &no_abort, g.status, KF_STATUS_TIMEOUT_PRODUCER);
+      if (lane == 0) {  // let every copy that was issued land before the CTA can exit
+        armed_st.drain(full, G1_S, g.status);
+        armed_ss.drain(sfull, kScaleRing, g.status);
       }
     } else if (warp == 1) {
       // -------------------------------------------------------- MMA issuer --
       if (lane == 0) {
         constexpr uint32_t idesc = idesc_e4m3_f32(128, 256);
-        int stage = 0, pb = 0;
-        uint32_t ph = 0, pph = 0;
+        RingPos st, pb;
         bool ok = true, committed = false;
-        int last_pb = 0;
-        uint32_t last_pph = 0;
+        RingPos last;
         for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
           for (int kb = 0; kb < kHB; ++kb) {
-            if (!mbar_wait_abort(&pempty[pb], pph ^ 1u, abort_flag, g.status, KF_STATUS_TIMEOUT_MMA) ||
-                !mbar_wait_abort(&full[stage], ph, abort_flag, g.status, KF_STATUS_TIMEOUT_MMA)) {
+            if (!mbar_wait_abort(&pempty[pb.idx], pb.ph ^ 1u, abort_flag, g.status, KF_STATUS_TIMEOUT_MMA) ||
+                !mbar_wait_abort(&full[st.idx], st.ph, abort_flag, g.status, KF_STATUS_TIMEOUT_MMA)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t a0 = smem_u32(sA + stage * G1_A);
-            const uint32_t b0 = smem_u32(sB + stage * G1_B);
-            const uint32_t d = tmem + static_cast<uint32_t>(pb * 256);
+            const uint32_t a0 = smem_u32(sA + st.idx * G1_A);
+            const uint32_t b0 = smem_u32(sB + st.idx * G1_B);
+            const uint32_t d = tmem + static_cast<uint32_t>(pb.idx * 256);
 #pragma unroll
             for (int k = 0; k < kBlk / 32; ++k)
               mma_f8(d, sw128_kmajor_desc(a0 + k * 32), sw128_kmajor_desc(b0 + k * 32), idesc, k > 0 ? 1u : 0u);
-            mma_commit(&empty[stage]);
-            mma_commit(&pfull[pb]);
+            mma_commit(&empty[st.idx]);
+            mma_commit(&pfull[pb.idx]);
             committed = true;
-            last_pb = pb;
-            last_pph = pph;
-            if (++stage == G1_S) {
-              stage = 0;
-              ph ^= 1u;
-            }
-            if (++pb == 2) {
-              pb = 0;
-              pph ^= 1u;
-            }
+            last = pb;
+            st.advance<G1_S>();
+            pb.advance<2>();
           }
         }
         if (committed) {  // the tensor core must be idle before TMEM is released
           int no_abort = 0;
-          mbar_wait_abort(&pfull[last_pb], last_pph, &no_abort, g.status, KF_STATUS_TIMEOUT_MMA);
+          mbar_wait_abort(&pfull[last.idx], last.ph, &no_abort, g.status, KF_STATUS_TIMEOUT_MMA);
         }
       }
       __syncwarp();
@@ -255,64 +282,62 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;       // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-    int stage = 0, pb = 0, it = 0;
-    uint32_t ph = 0, pph = 0;
+    RingPos ss, pb;
+    int it = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++it) {
       const int tile = u / kIB, nb = u % kIB;
       const int row0 = g.tile_row0[tile];
       const int nrows = g.tile_rows[tile];
-      float acc_u[64], acc_g[64];
+      const bool live = q * 32 < nrows;   // this warp's 32 rows hold at least one real pair
+      float2 acc_u[32], acc_g[32];
 #pragma unroll
-      for (int j = 0; j < 64; ++j) {
-        acc_u[j] = 0.f;
-        acc_g[j] = 0.f;
+      for (int j = 0; j < 32; ++j) {
+        acc_u[j] = make_float2(0.f, 0.f);
+        acc_g[j] = make_float2(0.f, 0.f);
       }
       for (int kb = 0; kb < kHB; ++kb) {
-        if (!mbar_wait_abort(&full[stage], ph, abort_flag, g.status, KF_STATUS_TIMEOUT_EPILOGUE)) {
+        if (!mbar_wait_abort(&sfull[ss.idx], ss.ph, abort_flag, g.status, KF_STATUS_TIMEOUT_EPILOGUE)) {
           ok = false;
           break;
         }
-        const float a_s = as_ring[stage * kBlk + row];
-        const float2 ws = ws_ring[stage];
+        const float a_s = as_ring[ss.idx * kBlk + row];
+        const float2 ws = ws_ring[ss.idx];
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[stage]);
-        if (!mbar_wait_abort(&pfull[pb], pph, abort_flag, g.status, KF_STATUS_TIMEOUT_EPILOGUE)) {
+        if (lane == 0) mbar_arrive(&sempty[ss.idx]);
+        if (!mbar_wait_abort(&pfull[pb.idx], pb.ph, abort_flag, g.status, KF_STATUS_TIMEOUT_EPILOGUE)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t taddr = tmem + lane_base + static_cast<uint32_t>(pb * 256 + h * 64);
-        float v[64];
-        tmem_ld64_sync(taddr, v);
-        const float su = a_s * ws.x;
+        if (live) {
+          const uint32_t taddr = tmem + lane_base + static_cast<uint32_t>(pb.idx * 256 + h * 64);
+          float v[64];
+          tmem_ld64_sync(taddr, v);
+          const float2 su = make_float2(a_s * ws.x, a_s * ws.x);
 #pragma unroll
-        for (int j = 0; j < 64; ++j) acc_u[j] = fmaf(v[j], su, acc_u[j]);
-        tmem_ld64_sync(taddr + 128, v);
-        const float sg = a_s * ws.y;
+          for (int j = 0; j < 32; ++j) acc_u[j] = __ffma2_rn(make_float2(v[2 * j], v[2 * j + 1]), su, acc_u[j]);
+          tmem_ld64_sync(taddr + 128, v);
+          const float2 sg = make_float2(a_s * ws.y, a_s * ws.y);
 #pragma unroll
-        for (int j = 0; j < 64; ++j) acc_g[j] = fmaf(v[j], sg, acc_g[j]);
+          for (int j = 0; j < 32; ++j) acc_g[j] = __ffma2_rn(make_float2(v[2 * j], v[2 * j + 1]), sg, acc_g[j]);
+        }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&pempty[pb]);
-        if (++stage == G1_S) {
-          stage = 0;
-          ph ^= 1u;
-        }
-        if (++pb == 2) {
-          pb = 0;
-          pph ^= 1u;
-        }
+        if (lane == 0) mbar_arrive(&pempty[pb.idx]);
+        ss.advance<kScaleRing>();
+        pb.advance<2>();
       }
       if (!ok) break;
       // SwiGLU: silu(X2) * X1 with X1 = up (W13 rows [0, I)), X2 = gate (rows [I, 2I))
       float amax = 0.f;
 #pragma unroll
-      for (int j = 0; j < 64; ++j) {
-        const float gt = acc_g[j];
-        const float hv = (gt / (1.0f + expf(-gt))) * acc_u[j];
-        acc_u[j] = hv;
-        amax = fmaxf(amax, fabsf(hv));
+      for (int j = 0; j < 32; ++j) {
+        const float2 gt = acc_g[j];
+        const float hx = (gt.x / (1.0f + expf(-gt.x))) * acc_u[j].x;
+        const float hy = (gt.y / (1.0f + expf(-gt.y))) * acc_u[j].y;
+        acc_u[j] = make_float2(hx, hy);
+        amax = fmaxf(amax, fmaxf(fabsf(hx), fabsf(hy)));
       }
       const int xb = it & 1;
       xch[(xb * 2 + h) * kBlk + row] = amax;
@@ -331,16 +356,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint4* dh = reinterpret_cast<uint4*>(g.c_hi + off);
         uint4* dl = reinterpret_cast<uint4*>(g.c_lo + off);
 #pragma unroll
-        for (int j = 0; j < 64; j += 16) {
-          const uint2 w0 = encode_hilo4(acc_u[j] * inv, acc_u[j + 1] * inv, acc_u[j + 2] * inv, acc_u[j + 3] * inv);
+        for (int j = 0; j < 32; j += 8) {
+          const uint2 w0 = encode_hilo4(acc_u[j].x * inv, acc_u[j].y * inv, acc_u[j + 1].x * inv, acc_u[j + 1].y * inv);
           const uint2 w1 =
-              encode_hilo4(acc_u[j + 4] * inv, acc_u[j + 5] * inv, acc_u[j + 6] * inv, acc_u[j + 7] * inv);
+              encode_hilo4(acc_u[j + 2].x * inv, acc_u[j + 2].y * inv, acc_u[j + 3].x * inv, acc_u[j + 3].y * inv);
           const uint2 w2 =
-              encode_hilo4(acc_u[j + 8] * inv, acc_u[j + 9] * inv, acc_u[j + 10] * inv, acc_u[j + 11] * inv);
+              encode_hilo4(acc_u[j + 4].x * inv, acc_u[j + 4].y * inv, acc_u[j + 5].x * inv, acc_u[j + 5].y * inv);
           const uint2 w3 =
-              encode_hilo4(acc_u[j + 12] * inv, acc_u[j + 13] * inv, acc_u[j + 14] * inv, acc_u[j + 15] * inv);
-          dh[j / 16] = make_uint4(w0.x, w1.x, w2.x, w3.x);
-          dl[j / 16] = make_uint4(w0.y, w1.y, w2.y, w3.y);
+              encode_hilo4(acc_u[j + 6].x * inv, acc_u[j + 6].y * inv, acc_u[j + 7].x * inv, acc_u[j + 7].y * inv);
+          dh[j / 8] = make_uint4(w0.x, w1.x, w2.x, w3.x);
+          dl[j / 8] = make_uint4(w0.y, w1.y, w2.y, w3.y);
         }
         if (h == 0) g.c_scale[static_cast<size_t>(nb) * g.p_cap + row0 + row] = scale;
       }
@@ -355,6 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 __global__ void __launch_bounds__(kThreads, 1)
     gemm2_weighted_kernel(const __grid_constant__ CUtensorMap tm_chi, const __grid_constant__ CUtensorMap tm_clo,
+                          const __grid_constant__ CUtensorMap tm_chi32, const __grid_constant__ CUtensorMap tm_clo32,
                           const __grid_constant__ CUtensorMap tm_w, const Gemm2Args g) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -365,8 +391,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   float2* ws_ring = reinterpret_cast<float2*>(smem + G2_OFF_WS);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G2_OFF_BAR);
   uint64_t* full = bars;
-  uint64_t* empty = bars + G2_S;
-  uint64_t* pfull = bars + 2 * G2_S;
+  uint64_t* empty = full + G2_S;
+  uint64_t* sfull = empty + G2_S;
+  uint64_t* sempty = sfull + kScaleRing;
+  uint64_t* pfull = sempty + kScaleRing;
   uint64_t* pempty = pfull + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + G2_OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + G2_OFF_MISC + 4);
@@ -378,7 +406,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < G2_S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1 + kEpiWarps);
+      mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < kScaleRing; ++s) {
+      mbar_init(&sfull[s], 1);
+      mbar_init(&sempty[s], kEpiWarps);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&pfull[b], 1);
@@ -390,6 +422,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_chi);
     tma_prefetch_desc(&tm_clo);
+    tma_prefetch_desc(&tm_chi32);
+    tma_prefetch_desc(&tm_clo32);
     tma_prefetch_desc(&tm_w);
   }
   if (warp == 1) tmem_alloc(tmem_holder, 512);
@@ -401,13 +435,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp < 4) {
     setmaxnreg_dec<kRegsLow>();
     if (warp == 0) {
-      int stage = 0;
-      uint32_t ph = 0, armed = 0, armed_par = 0;
+      RingPos st, ss;
+      ArmedSlots armed_st, armed_ss;
       bool ok = true;
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
         const int tile = u / kG2NB, nb2 = u % kG2NB;
         const int e = g.tile_expert[tile];
         const int row0 = g.tile_row0[tile];
+        const bool small = g.tile_rows[tile] <= kSmallRows;
+        const uint32_t tx = 2 * (small ? kSmallRows * kBlk : G2_A) + G2_B;
         // w2_scale[e][nb][kb], nb = 2*nb2 + {0,1}, kb in [0,16): lane kb holds both
         const float* ws = g.w2_scale + (static_cast<size_t>(e) * kHB + 2 * nb2) * kIB;
         const float s0 = lane < kIB ? ws[lane] : 0.f;
@@ -418,17 +454,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float w1 = __shfl_sync(0xffffffffu, s1, kb);
           int good = 1;
           if (lane == 0) {
-            good = mbar_wait_abort(&empty[stage], ph ^ 1u, abort_flag, g.status, KF_STATUS_TIMEOUT_PRODUCER);
+            good = mbar_wait_abort(&empty[st.idx], st.ph ^ 1u, abort_flag, g.status, KF_STATUS_TIMEOUT_PRODUCER) &&
+                   mbar_wait_abort(&sempty[ss.idx], ss.ph ^ 1u, abort_flag, g.status, KF_STATUS_TIMEOUT_PRODUCER);
             if (good) {
-              ws_ring[stage] = make_float2(w0, w1);
-              mbar_arrive_expect_tx(&full[stage], G2_TX);
-              tma_load_2d(sAhi + stage * G2_A, &tm_chi, kb * kBlk, row0, &full[stage]);
-              tma_load_2d(sAlo + stage * G2_A, &tm_clo, kb * kBlk, row0, &full[stage]);
-              tma_load_2d(sB + stage * G2_B, &tm_w, kb * kBlk, wrow, &full[stage]);
-              bulk_load(as_ring + stage * kBlk, g.c_scale + static_cast<size_t>(kb) * g.p_cap + row0, kBlk * 4,
-                        &full[stage]);
-              armed |= 1u << stage;
-              armed_par = ph ? (armed_par | (1u << stage)) : (armed_par & ~(1u << stage));
+              ws_ring[ss.idx] = make_float2(w0, w1);
+              mbar_arrive_expect_tx(&sfull[ss.idx], kBlk * 4);
+              bulk_load(as_ring + ss.idx * kBlk, g.c_scale + static_cast<size_t>(kb) * g.p_cap + row0, kBlk * 4,
+                        &sfull[ss.idx]);
+              armed_ss.set(ss.idx, ss.ph);
+              mbar_arrive_expect_tx(&full[st.idx], tx);
+              tma_load_2d(sAhi + st.idx * G2_A, small ? &tm_chi32 : &tm_chi, kb * kBlk, row0, &full[st.idx]);
+              tma_load_2d(sAlo + st.idx * G2_A, small ? &tm_clo32 : &tm_clo, kb * kBlk, row0, &full[st.idx]);
+              tma_load_2d(sB + st.idx * G2_B, &tm_w, kb * kBlk, wrow, &full[st.idx]);
+              armed_st.set(st.idx, st.ph);
             }
           }
           good = __shfl_sync(0xffffffffu, good, 0);
@@ -436,62 +474,48 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          if (++stage == G2_S) {
-            stage = 0;
-            ph ^= 1u;
-          }
+          st.advance<G2_S>();
+          ss.advance<kScaleRing>();
         }
       }
       if (lane == 0) {
-        int no_abort = 0;
-        for (int s = 0; s < G2_S; ++s)
-          if ((armed >> s) & 1u)
-            mbar_wait_abort(&full[s], (armed_par >> s) & 1u, &no_abort, g.status, KF_STATUS_TIMEOUT_PRODUCER);
+        armed_st.drain(full, G2_S, g.status);
+        armed_ss.drain(sfull, kScaleRing, g.status);
       }
     } else if (warp == 1) {
       if (lane == 0) {
         constexpr uint32_t idesc = idesc_e4m3_f32(128, 256);
-        int stage = 0, pb = 0;
-        uint32_t ph = 0, pph = 0;
+        RingPos st, pb, last;
         bool ok = true, committed = false;
-        int last_pb = 0;
-        uint32_t last_pph = 0;
         for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
           for (int kb = 0; kb < kIB; ++kb) {
-            if (!mbar_wait_abort(&pempty[pb], pph ^ 1u, abort_flag, g.status, KF_STATUS_TIMEOUT_MMA) ||
-                !mbar_wait_abort(&full[stage], ph, abort_flag, g.status, KF_STATUS_TIMEOUT_MMA)) {
+            if (!mbar_wait_abort(&pempty[pb.idx], pb.ph ^ 1u, abort_flag, g.status, KF_STATUS_TIMEOUT_MMA) ||
+                !mbar_wait_abort(&full[st.idx], st.ph, abort_flag, g.status, KF_STATUS_TIMEOUT_MMA)) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t ahi = smem_u32(sAhi + stage * G2_A);
-            const uint32_t alo = smem_u32(sAlo + stage * G2_A);
-            const uint32_t b0 = smem_u32(sB + stage * G2_B);
-            const uint32_t d = tmem + static_cast<uint32_t>(pb * 256);
+            const uint32_t ahi = smem_u32(sAhi + st.idx * G2_A);
+            const uint32_t alo = smem_u32(sAlo + st.idx * G2_A);
+            const uint32_t b0 = smem_u32(sB + st.idx * G2_B);
+            const uint32_t d = tmem + static_cast<uint32_t>(pb.idx * 256);
 #pragma unroll
             for (int k = 0; k < kBlk / 32; ++k) {
               const uint64_t bd = sw128_kmajor_desc(b0 + k * 32);
               mma_f8(d, sw128_kmajor_desc(ahi + k * 32), bd, idesc, k > 0 ? 1u : 0u);
               mma_f8(d, sw128_kmajor_desc(alo + k * 32), bd, idesc, 1u);
             }
-            mma_commit(&empty[stage]);
-            mma_commit(&pfull[pb]);
+            mma_commit(&empty[st.idx]);
+            mma_commit(&pfull[pb.idx]);
             committed = true;
-            last_pb = pb;
-            last_pph = pph;
-            if (++stage == G2_S) {
-              stage = 0;
-              ph ^= 1u;
-            }
-            if (++pb == 2) {
-              pb = 0;
-              pph ^= 1u;
-            }
+            last = pb;
+            st.advance<G2_S>();
+            pb.advance<2>();
           }
         }
         if (committed) {
           int no_abort = 0;
-          mbar_wait_abort(&pfull[last_pb], last_pph, &no_abort, g.status, KF_STATUS_TIMEOUT_MMA);
+          mbar_wait_abort(&pfull[last.idx], last.ph, &no_abort, g.status, KF_STATUS_TIMEOUT_MMA);
         }
       }
       __syncwarp();
@@ -503,58 +527,56 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const int row = q * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-    int stage = 0, pb = 0;
-    uint32_t ph = 0, pph = 0;
+    RingPos ss, pb;
     bool ok = true;
     for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
       const int tile = u / kG2NB, nb2 = u % kG2NB;
       const int row0 = g.tile_row0[tile];
       const int nrows = g.tile_rows[tile];
-      float acc[128];
+      const bool live = q * 32 < nrows;
+      float2 acc[64];
 #pragma unroll
-      for (int j = 0; j < 128; ++j) acc[j] = 0.f;
+      for (int j = 0; j < 64; ++j) acc[j] = make_float2(0.f, 0.f);
       for (int kb = 0; kb < kIB; ++kb) {
-        if (!mbar_wait_abort(&full[stage], ph, abort_flag, g.status, KF_STATUS_TIMEOUT_EPILOGUE)) {
+        if (!mbar_wait_abort(&sfull[ss.idx], ss.ph, abort_flag, g.status, KF_STATUS_TIMEOUT_EPILOGUE)) {
           ok = false;
           break;
         }
-        const float a_s = as_ring[stage * kBlk + row];
-        const float2 ws = ws_ring[stage];
+        const float a_s = as_ring[ss.idx * kBlk + row];
+        const float2 ws = ws_ring[ss.idx];
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[stage]);
-        if (!mbar_wait_abort(&pfull[pb], pph, abort_flag, g.status, KF_STATUS_TIMEOUT_EPILOGUE)) {
+        if (lane == 0) mbar_arrive(&sempty[ss.idx]);
+        if (!mbar_wait_abort(&pfull[pb.idx], pb.ph, abort_flag, g.status, KF_STATUS_TIMEOUT_EPILOGUE)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t taddr = tmem + lane_base + static_cast<uint32_t>(pb * 256 + h * 128);
-        const float sc = a_s * (h ? ws.y : ws.x);
-        float v[64];
-        tmem_ld64_sync(taddr, v);
+        if (live) {
+          const uint32_t taddr = tmem + lane_base + static_cast<uint32_t>(pb.idx * 256 + h * 128);
+          const float sc = a_s * (h ? ws.y : ws.x);
+          const float2 s2 = make_float2(sc, sc);
+          float v[64];
+          tmem_ld64_sync(taddr, v);
 #pragma unroll
-        for (int j = 0; j < 64; ++j) acc[j] = fmaf(v[j], sc, acc[j]);
-        tmem_ld64_sync(taddr + 64, v);
+          for (int j = 0; j < 32; ++j) acc[j] = __ffma2_rn(make_float2(v[2 * j], v[2 * j + 1]), s2, acc[j]);
+          tmem_ld64_sync(taddr + 64, v);
 #pragma unroll
-        for (int j = 0; j < 64; ++j) acc[64 + j] = fmaf(v[j], sc, acc[64 + j]);
+          for (int j = 0; j < 32; ++j)
+            acc[32 + j] = __ffma2_rn(make_float2(v[2 * j], v[2 * j + 1]), s2, acc[32 + j]);
+        }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&pempty[pb]);
-        if (++stage == G2_S) {
-          stage = 0;
-          ph ^= 1u;
-        }
-        if (++pb == 2) {
-          pb = 0;
-          pph ^= 1u;
-        }
+        if (lane == 0) mbar_arrive(&pempty[pb.idx]);
+        ss.advance<kScaleRing>();
+        pb.advance<2>();
       }
       if (!ok) break;
       if (row < nrows) {
         const float w = g.slot_weight[row0 + row];
         float4* dst = reinterpret_cast<float4*>(g.y + static_cast<size_t>(row0 + row) * kH + nb2 * 256 + h * 128);
 #pragma unroll
-        for (int j = 0; j < 128; j += 4)
-          dst[j / 4] = make_float4(acc[j] * w, acc[j + 1] * w, acc[j + 2] * w, acc[j + 3] * w);
+        for (int j = 0; j < 64; j += 2)
+          dst[j / 2] = make_float4(acc[j].x * w, acc[j].y * w, acc[j + 1].x * w, acc[j + 1].y * w);
       }
     }
   }
@@ -573,15 +595,16 @@ cudaError_t gemm_set_attributes() {
   return cudaFuncSetAttribute(gemm2_weighted_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, G2_SMEM);
 }
 
-cudaError_t launch_gemm1(const CUtensorMap& tm_a, const CUtensorMap& tm_w13, const Gemm1Args& args, int grid,
-                         cudaStream_t s) {
-  gemm1_swiglu_kernel<<<grid, kThreads, G1_SMEM, s>>>(tm_a, tm_w13, args);
+cudaError_t launch_gemm1(const CUtensorMap& tm_a, const CUtensorMap& tm_a32, const CUtensorMap& tm_w13,
+                         const Gemm1Args& args, int grid, cudaStream_t s) {
+  gemm1_swiglu_kernel<<<grid, kThreads, G1_SMEM, s>>>(tm_a, tm_a32, tm_w13, args);
   return cudaGetLastError();
 }
 
-cudaError_t launch_gemm2(const CUtensorMap& tm_chi, const CUtensorMap& tm_clo, const CUtensorMap& tm_w2,
-                         const Gemm2Args& args, int grid, cudaStream_t s) {
-  gemm2_weighted_kernel<<<grid, kThreads, G2_SMEM, s>>>(tm_chi, tm_clo, tm_w2, args);
+cudaError_t launch_gemm2(const CUtensorMap& tm_chi, const CUtensorMap& tm_clo, const CUtensorMap& tm_chi32,
+                         const CUtensorMap& tm_clo32, const CUtensorMap& tm_w2, const Gemm2Args& args, int grid,
+                         cudaStream_t s) {
+  gemm2_weighted_kernel<<<grid, kThreads, G2_SMEM, s>>>(tm_chi, tm_clo, tm_chi32, tm_clo32, tm_w2, args);
   return cudaGetLastError();
 }
 

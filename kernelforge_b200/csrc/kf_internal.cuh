@@ -92,10 +92,11 @@ struct Gemm2Args {
   int* status;
 };
 
-cudaError_t launch_gemm1(const CUtensorMap& tm_a, const CUtensorMap& tm_w13, const Gemm1Args& args, int grid,
+cudaError_t launch_gemm1(const CUtensorMap& tm_a, const CUtensorMap& tm_a32, const CUtensorMap& tm_w13,
+                         const Gemm1Args& args, int grid, cudaStream_t s);
+cudaError_t launch_gemm2(const CUtensorMap& tm_chi, const CUtensorMap& tm_clo, const CUtensorMap& tm_chi32,
+                         const CUtensorMap& tm_clo32, const CUtensorMap& tm_w2, const Gemm2Args& args, int grid,
                          cudaStream_t s);
-cudaError_t launch_gemm2(const CUtensorMap& tm_chi, const CUtensorMap& tm_clo, const CUtensorMap& tm_w2,
-                         const Gemm2Args& args, int grid, cudaStream_t s);
 cudaError_t gemm_set_attributes();
 
 }  // namespace kf

@@ -96,8 +96,8 @@ int ensure_device(int* num_sms) {
 }
 
 // Row-major [outer, inner] bytes, box [box_outer, box_inner], 128-byte swizzle.
-bool encode_u8_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
-                  uint32_t box_outer) {
+bool encode_u8_2d_uncached(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
+                           uint32_t box_outer) {
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {inner};
   const cuuint32_t box[2] = {box_inner, box_outer};
@@ -106,6 +106,38 @@ bool encode_u8_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t o
                               elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+// Tensor maps depend only on (base, shape, box); repeated calls with the same
+// weights and workspace reuse the encoded maps.
+struct MapCacheEntry {
+  const void* base;
+  uint64_t inner, outer;
+  uint32_t box_inner, box_outer;
+  CUtensorMap map;
+};
+constexpr int kMapCache = 64;
+MapCacheEntry g_maps[kMapCache];
+int g_maps_used = 0, g_maps_next = 0;
+std::mutex g_maps_mu;
+
+bool encode_u8_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
+                  uint32_t box_outer) {
+  std::lock_guard<std::mutex> lock(g_maps_mu);
+  for (int i = 0; i < g_maps_used; ++i) {
+    const MapCacheEntry& c = g_maps[i];
+    if (c.base == base && c.inner == inner && c.outer == outer && c.box_inner == box_inner &&
+        c.box_outer == box_outer) {
+      *map = c.map;
+      return true;
+    }
+  }
+  if (!encode_u8_2d_uncached(map, base, inner, outer, box_inner, box_outer)) return false;
+  MapCacheEntry& c = g_maps[g_maps_next];
+  c = MapCacheEntry{base, inner, outer, box_inner, box_outer, *map};
+  g_maps_next = (g_maps_next + 1) % kMapCache;
+  if (g_maps_used < kMapCache) ++g_maps_used;
+  return true;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -147,11 +179,16 @@ int run_experts(const Workspace& w, void* ws, const int32_t* topk_idx, const flo
       return KF_ERR_CUDA;
   }
 
-  CUtensorMap tm_a, tm_w13, tm_chi, tm_clo, tm_w2;
+  // Row tiles with <= 32 valid rows load only a 32-row A box (the MMA still spans
+  // 128 rows; the stale rows only feed accumulator rows that are never stored).
+  CUtensorMap tm_a, tm_a32, tm_w13, tm_chi, tm_clo, tm_chi32, tm_clo32, tm_w2;
   if (!encode_u8_2d(&tm_a, ws_ptr<uint8_t>(ws, w.a_rows), kH, w.p_cap, kBlk, kBlk) ||
+      !encode_u8_2d(&tm_a32, ws_ptr<uint8_t>(ws, w.a_rows), kH, w.p_cap, kBlk, 32) ||
       !encode_u8_2d(&tm_w13, w13, kH, static_cast<uint64_t>(E) * 2 * kI, kBlk, kBlk) ||
       !encode_u8_2d(&tm_chi, ws_ptr<uint8_t>(ws, w.c_hi), kI, w.p_cap, kBlk, kBlk) ||
       !encode_u8_2d(&tm_clo, ws_ptr<uint8_t>(ws, w.c_lo), kI, w.p_cap, kBlk, kBlk) ||
+      !encode_u8_2d(&tm_chi32, ws_ptr<uint8_t>(ws, w.c_hi), kI, w.p_cap, kBlk, 32) ||
+      !encode_u8_2d(&tm_clo32, ws_ptr<uint8_t>(ws, w.c_lo), kI, w.p_cap, kBlk, 32) ||
       !encode_u8_2d(&tm_w2, w2, kI, static_cast<uint64_t>(E) * kH, kBlk, 256))
     return KF_ERR_INVALID_ARGUMENT;
 
@@ -170,7 +207,7 @@ int run_experts(const Workspace& w, void* ws, const int32_t* topk_idx, const flo
   const int units1 = w.nt_cap * kIB;
   {
     ProfScope ps(KF_KERNEL_GEMM1, s);
-    if (launch_gemm1(tm_a, tm_w13, g1, units1 < num_sms ? units1 : num_sms, s) != cudaSuccess) return KF_ERR_CUDA;
+    if (launch_gemm1(tm_a, tm_a32, tm_w13, g1, units1 < num_sms ? units1 : num_sms, s) != cudaSuccess) return KF_ERR_CUDA;
   }
 
   Gemm2Args g2;
@@ -187,7 +224,7 @@ int run_experts(const Workspace& w, void* ws, const int32_t* topk_idx, const flo
   const int units2 = w.nt_cap * (kH / 256);
   {
     ProfScope ps(KF_KERNEL_GEMM2, s);
-    if (launch_gemm2(tm_chi, tm_clo, tm_w2, g2, units2 < num_sms ? units2 : num_sms, s) != cudaSuccess)
+    if (launch_gemm2(tm_chi, tm_clo, tm_chi32, tm_clo32, tm_w2, g2, units2 < num_sms ? units2 : num_sms, s) != cudaSuccess)
       return KF_ERR_CUDA;
   }
 

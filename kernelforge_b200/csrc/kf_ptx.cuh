@@ -152,9 +152,9 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                : "memory");
 }
 
-// 32 lanes x 64 consecutive 32-bit columns: thread i of the warp reads TMEM lane
-// (lane base + i).  The load and its wait sit in one asm block, so the compiler
-// cannot consume the registers before the data has arrived.
+// 32 lanes x N consecutive 32-bit columns (N = 32 or 64): thread i of the warp
+// reads TMEM lane (lane base + i).  The load and its wait sit in one asm block,
+// so the compiler cannot consume the registers before the data has arrived.
 __device__ __forceinline__ void tmem_ld64_sync(uint32_t taddr, float (&v)[64]) {
   uint32_t r[64];
   asm volatile(
@@ -166,6 +166,19 @@ __device__ __forceinline__ void tmem_ld64_sync(uint32_t taddr, float (&v)[64]) {
       : "memory");
 #pragma unroll
   for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_ld32_sync(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]),"=r"(r[1]),"=r"(r[2]),"=r"(r[3]),"=r"(r[4]),"=r"(r[5]),"=r"(r[6]),"=r"(r[7]),"=r"(r[8]),"=r"(r[9]),"=r"(r[10]),"=r"(r[11]),"=r"(r[12]),"=r"(r[13]),"=r"(r[14]),"=r"(r[15]),"=r"(r[16]),"=r"(r[17]),"=r"(r[18]),"=r"(r[19]),"=r"(r[20]),"=r"(r[21]),"=r"(r[22]),"=r"(r[23]),"=r"(r[24]),"=r"(r[25]),"=r"(r[26]),"=r"(r[27]),"=r"(r[28]),"=r"(r[29]),"=r"(r[30]),"=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // Shared-memory matrix descriptor for a K-major operand tile written by TMA with

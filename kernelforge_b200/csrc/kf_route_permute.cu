@@ -19,25 +19,23 @@ namespace kf {
 
 namespace {
 
-constexpr int kRouteThreads = 1024;  // 32 warps, 4 tokens each per chunk of 128
+constexpr int kRouteThreads = 256;  // 8 warps, one token each
 
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
   return v > bv || (v == bv && i < bi);
 }
 
 // One warp routes one token.  Lane l owns experts [8l, 8l+8); group g = lanes [4g, 4g+4).
+// With chunk_masks (zeroed beforehand), the token's bit is set in the mask of
+// each selected local expert for the token's chunk of 128.
 __global__ void __launch_bounds__(kRouteThreads) route_kernel(const float* __restrict__ logits,
                                                               const __nv_bfloat16* __restrict__ bias, int T,
                                                               float rsf, int32_t* __restrict__ topk_idx,
                                                               float* __restrict__ topk_w, int E, int offset,
-                                                              uint4* __restrict__ chunk_masks) {
-  __shared__ uint32_t masks[kMaxLocalExperts * 4];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int chunk = blockIdx.x;
-  if (chunk_masks) {
-    for (int i = threadIdx.x; i < E * 4; i += blockDim.x) masks[i] = 0u;
-    __syncthreads();
-  }
+                                                              uint32_t* __restrict__ chunk_masks) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (kRouteThreads / 32) + (threadIdx.x >> 5);
+  if (t >= T) return;
   float b[8];
   {
     const uint4 raw = *reinterpret_cast<const uint4*>(bias + lane * 8);
@@ -49,9 +47,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const float* __res
       b[2 * j + 1] = f.y;
     }
   }
-  for (int tl = warp; tl < kChunkTokens; tl += kRouteThreads / 32) {
-    const int t = chunk * kChunkTokens + tl;
-    if (t >= T) break;
+  {
     const float4* lp = reinterpret_cast<const float4*>(logits + static_cast<size_t>(t) * kEG + lane * 8);
     const float4 x0 = lp[0], x1 = lp[1];
     const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
@@ -158,15 +154,11 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const float* __res
       topk_w[static_cast<size_t>(t) * kTopK + lane] = w;
       if (chunk_masks) {
         const int le = e - offset;
-        if (le >= 0 && le < E) atomicOr(&masks[le * 4 + (tl >> 5)], 1u << (tl & 31));
+        const int tl = t & (kChunkTokens - 1);
+        if (le >= 0 && le < E)
+          atomicOr(&chunk_masks[(static_cast<size_t>(t / kChunkTokens) * E + le) * 4 + (tl >> 5)], 1u << (tl & 31));
       }
     }
-  }
-  if (chunk_masks) {
-    __syncthreads();
-    uint4* dst = chunk_masks + static_cast<size_t>(chunk) * E;
-    for (int e = threadIdx.x; e < E; e += blockDim.x)
-      dst[e] = make_uint4(masks[e * 4], masks[e * 4 + 1], masks[e * 4 + 2], masks[e * 4 + 3]);
   }
 }
 
@@ -389,9 +381,15 @@ __global__ void __launch_bounds__(256) unpermute_reduce_kernel(const int32_t* __
 
 cudaError_t launch_route(const float* logits, const void* bias, int T, float rsf, int32_t* topk_idx,
                          float* topk_w, int E, int offset, uint4* chunk_masks, cudaStream_t s) {
-  const int nchunk = (T + kChunkTokens - 1) / kChunkTokens;
-  route_kernel<<<nchunk, kRouteThreads, 0, s>>>(logits, static_cast<const __nv_bfloat16*>(bias), T, rsf, topk_idx,
-                                                topk_w, E, offset, chunk_masks);
+  if (chunk_masks) {
+    const int nchunk = (T + kChunkTokens - 1) / kChunkTokens;
+    const cudaError_t e = cudaMemsetAsync(chunk_masks, 0, static_cast<size_t>(nchunk) * E * sizeof(uint4), s);
+    if (e != cudaSuccess) return e;
+  }
+  const int warps = kRouteThreads / 32;
+  route_kernel<<<(T + warps - 1) / warps, kRouteThreads, 0, s>>>(logits, static_cast<const __nv_bfloat16*>(bias), T,
+                                                                 rsf, topk_idx, topk_w, E, offset,
+                                                                 reinterpret_cast<uint32_t*>(chunk_masks));
   return cudaGetLastError();
 }
 
