@@ -122,7 +122,7 @@ int kf_moe_read_status(void* workspace, int32_t* status, void* stream);
 /* Limits of kf_moe_forward_noalloc and the size of its static scratch array. */
 #define KF_MOE_NOALLOC_MAX_TOKENS 16
 #define KF_MOE_NOALLOC_MAX_LOCAL_EXPERTS 32
-#define KF_MOE_NOALLOC_SCRATCH_BYTES (163u << 20) /* 163 MiB */
+#define KF_MOE_NOALLOC_SCRATCH_BYTES (168u << 20) /* 168 MiB */
 
 /*
  * kf_moe_forward for callers that cannot allocate device memory.  This entry

@@ -19,12 +19,13 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libkf_moe.so")
-SOURCES = ["kf_route_permute.cu", "kf_grouped_gemm.cu", "kf_moe_api.cu", "kf_moe_noalloc.cu"]
+SOURCES = ["kf_route_permute.cu", "kf_grouped_gemm.cu", "kf_grouped_gemm_pair.cu", "kf_moe_api.cu",
+           "kf_moe_noalloc.cu"]
 HEADERS = ["kf_ptx.cuh", "kf_internal.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xptxas", "-v", f"-I{INCLUDE}"]
-SETMAXNREG_KERNELS = ("gemm1_swiglu_kernel", "gemm2_weighted_kernel")
+SETMAXNREG_KERNELS = ("gemm1_swiglu_kernel", "gemm2_weighted_kernel", "gemm1_pair_kernel", "gemm2_pair_kernel")
 REQUIRED_REGS = 168
 
 

@@ -24,7 +24,8 @@ constexpr int kMaxLocalExperts = 256;
 struct Meta {
   int32_t num_tiles;       // row tiles of 128 permuted rows, over all local experts
   int32_t num_pairs;       // local (token, expert) pairs
-  int32_t reserved[62];
+  int32_t num_ptiles;      // pair tiles of 256 rows (two CTAs of a 2-SM MMA), over all local experts
+  int32_t reserved[61];
   int32_t expert_count[kMaxLocalExperts];      // pairs per local expert
   int32_t expert_pad_start[kMaxLocalExperts];  // first permuted row of each expert (128-aligned)
 };
@@ -32,7 +33,7 @@ struct Meta {
 // Offsets (bytes) of every scratch array inside the caller's workspace.
 struct Workspace {
   size_t status, meta, topk_idx, topk_w, token_slot, chunk_masks, chunk_base;
-  size_t tile_expert, tile_row0, tile_rows, slot_token, slot_weight;
+  size_t tile_expert, tile_row0, tile_rows, ptile_expert, ptile_row0, ptile_rows, slot_token, slot_weight;
   size_t a_rows, a_scale, c_hi, c_lo, c_scale, y;
   size_t total;
   int32_t p_cap;    // capacity in permuted rows (multiple of 128)
@@ -53,8 +54,8 @@ cudaError_t launch_route(const float* logits, const void* bias, int T, float rsf
 cudaError_t launch_masks_from_topk(const int32_t* topk_idx, int T, int E, int offset, uint4* chunk_masks,
                                    int* status, cudaStream_t s);
 cudaError_t launch_permute_scan(const uint4* chunk_masks, int nchunk, int E, Meta* meta, int32_t* chunk_base,
-                                int32_t* tile_expert, int32_t* tile_row0, int32_t* tile_rows, int nt_cap,
-                                int* status, cudaStream_t s);
+                                int32_t* tile_expert, int32_t* tile_row0, int32_t* tile_rows, int32_t* ptile_expert,
+                                int32_t* ptile_row0, int32_t* ptile_rows, int nt_cap, int* status, cudaStream_t s);
 cudaError_t launch_permute_assign(const int32_t* topk_idx, const float* topk_w, const uint4* chunk_masks,
                                   const int32_t* chunk_base, const Meta* meta, int T, int E, int offset, int p_cap,
                                   int32_t* token_slot, int32_t* slot_token, float* slot_weight, int* status,
@@ -65,6 +66,8 @@ cudaError_t launch_gather_rows(const Meta* meta, const int32_t* tile_rows, const
 cudaError_t launch_reduce(const int32_t* token_slot, const float* y, int T, void* out, int out_fp32,
                           cudaStream_t s);
 
+// The tile fields hold 128-row tiles for the single-CTA kernels and 256-row pair
+// tiles for the CTA-pair kernels.
 struct Gemm1Args {
   const Meta* meta;
   const int32_t* tile_expert;
@@ -97,6 +100,14 @@ cudaError_t launch_gemm1(const CUtensorMap& tm_a, const CUtensorMap& tm_a32, con
 cudaError_t launch_gemm2(const CUtensorMap& tm_chi, const CUtensorMap& tm_clo, const CUtensorMap& tm_chi32,
                          const CUtensorMap& tm_clo32, const CUtensorMap& tm_w2, const Gemm2Args& args, int grid,
                          cudaStream_t s);
+cudaError_t launch_gemm1_pair(const CUtensorMap& tm_a, const CUtensorMap& tm_a32, const CUtensorMap& tm_w13,
+                              const Gemm1Args& args, int grid, cudaStream_t s);
+cudaError_t launch_gemm2_pair(const CUtensorMap& tm_chi, const CUtensorMap& tm_clo, const CUtensorMap& tm_chi32,
+                              const CUtensorMap& tm_clo32, const CUtensorMap& tm_w2, const Gemm2Args& args, int grid,
+                              cudaStream_t s);
 cudaError_t gemm_set_attributes();
+cudaError_t gemm_pair_set_attributes();
+// Co-resident 2-CTA clusters of the pair kernels on the current device (0 if unknown).
+int gemm_pair_max_clusters();
 
 }  // namespace kf

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -23,6 +24,7 @@ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 struct DeviceInfo {
   bool ready = false;
   int num_sms = 0;
+  int pair_clusters = 0;  // co-resident 2-CTA clusters of the CTA-pair GEMMs (0: use single-CTA GEMMs)
   int status = KF_OK;
 };
 
@@ -62,7 +64,13 @@ struct ProfScope {
   }
 };
 
-int ensure_device(int* num_sms) {
+// KF_MOE_GEMM=1sm selects the single-CTA GEMMs (for comparison); the default is the CTA-pair GEMMs.
+bool pair_gemms_requested() {
+  const char* v = getenv("KF_MOE_GEMM");
+  return !(v && strcmp(v, "1sm") == 0);
+}
+
+int ensure_device(int* num_sms, int* pair_clusters = nullptr) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return KF_ERR_CUDA;
   std::lock_guard<std::mutex> lock(g_mu);
@@ -74,10 +82,11 @@ int ensure_device(int* num_sms) {
     cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev);
     if (major != 10 || minor != 0) {
       d.status = KF_ERR_UNSUPPORTED_DEVICE;
-    } else if (gemm_set_attributes() != cudaSuccess) {
+    } else if (gemm_set_attributes() != cudaSuccess || gemm_pair_set_attributes() != cudaSuccess) {
       d.status = KF_ERR_CUDA;
     } else {
       d.status = KF_OK;
+      d.pair_clusters = pair_gemms_requested() ? gemm_pair_max_clusters() : 0;
     }
     if (!g_encode && d.status == KF_OK) {
       void* fn = nullptr;
@@ -92,6 +101,7 @@ int ensure_device(int* num_sms) {
     d.ready = true;
   }
   *num_sms = d.num_sms;
+  if (pair_clusters) *pair_clusters = d.pair_clusters;
   return d.status;
 }
 
@@ -152,14 +162,16 @@ int check_common(int32_t T, int32_t E, int32_t offset) {
 int run_experts(const Workspace& w, void* ws, const int32_t* topk_idx, const float* topk_w, const void* hidden,
                 const float* hidden_scale, const void* w13, const float* w13_scale, const void* w2,
                 const float* w2_scale, int T, int E, int offset, void* out, int out_fp32, int num_sms,
-                cudaStream_t s) {
+                int pair_clusters, cudaStream_t s) {
   int* status = ws_ptr<int>(ws, w.status);
   Meta* meta = ws_ptr<Meta>(ws, w.meta);
   {
     ProfScope ps(KF_KERNEL_PERMUTE_SCAN, s);
     if (launch_permute_scan(ws_ptr<uint4>(ws, w.chunk_masks), w.nchunk, E, meta, ws_ptr<int32_t>(ws, w.chunk_base),
                             ws_ptr<int32_t>(ws, w.tile_expert), ws_ptr<int32_t>(ws, w.tile_row0),
-                            ws_ptr<int32_t>(ws, w.tile_rows), w.nt_cap, status, s) != cudaSuccess)
+                            ws_ptr<int32_t>(ws, w.tile_rows), ws_ptr<int32_t>(ws, w.ptile_expert),
+                            ws_ptr<int32_t>(ws, w.ptile_row0), ws_ptr<int32_t>(ws, w.ptile_rows), w.nt_cap, status,
+                            s) != cudaSuccess)
       return KF_ERR_CUDA;
   }
   {
@@ -191,12 +203,22 @@ int run_experts(const Workspace& w, void* ws, const int32_t* topk_idx, const flo
       !encode_u8_2d(&tm_clo32, ws_ptr<uint8_t>(ws, w.c_lo), kI, w.p_cap, kBlk, 32) ||
       !encode_u8_2d(&tm_w2, w2, kI, static_cast<uint64_t>(E) * kH, kBlk, 256))
     return KF_ERR_INVALID_ARGUMENT;
+  // The CTA-pair GEMM2 loads half of the 256-row W2 tile per CTA: a 128-row box
+  // (its shared-memory slot holds exactly 128 rows).
+  CUtensorMap tm_w2_half;
+  if (pair_clusters > 0 && !encode_u8_2d(&tm_w2_half, w2, kI, static_cast<uint64_t>(E) * kH, kBlk, kBlk))
+    return KF_ERR_INVALID_ARGUMENT;
 
+  // CTA-pair GEMMs walk 256-row pair tiles, single-CTA GEMMs 128-row tiles.
+  const bool pair = pair_clusters > 0;
+  const int32_t* t_exp = ws_ptr<int32_t>(ws, pair ? w.ptile_expert : w.tile_expert);
+  const int32_t* t_row0 = ws_ptr<int32_t>(ws, pair ? w.ptile_row0 : w.tile_row0);
+  const int32_t* t_rows = ws_ptr<int32_t>(ws, pair ? w.ptile_rows : w.tile_rows);
   Gemm1Args g1;
   g1.meta = meta;
-  g1.tile_expert = ws_ptr<int32_t>(ws, w.tile_expert);
-  g1.tile_row0 = ws_ptr<int32_t>(ws, w.tile_row0);
-  g1.tile_rows = ws_ptr<int32_t>(ws, w.tile_rows);
+  g1.tile_expert = t_exp;
+  g1.tile_row0 = t_row0;
+  g1.tile_rows = t_rows;
   g1.a_scale = ws_ptr<float>(ws, w.a_scale);
   g1.w13_scale = w13_scale;
   g1.c_hi = ws_ptr<uint8_t>(ws, w.c_hi);
@@ -204,28 +226,42 @@ int run_experts(const Workspace& w, void* ws, const int32_t* topk_idx, const flo
   g1.c_scale = ws_ptr<float>(ws, w.c_scale);
   g1.p_cap = w.p_cap;
   g1.status = status;
-  const int units1 = w.nt_cap * kIB;
   {
     ProfScope ps(KF_KERNEL_GEMM1, s);
-    if (launch_gemm1(tm_a, tm_a32, tm_w13, g1, units1 < num_sms ? units1 : num_sms, s) != cudaSuccess) return KF_ERR_CUDA;
+    cudaError_t e;
+    if (pair) {
+      const int units = w.nt_cap * kIB;
+      const int clusters = units < pair_clusters ? units : pair_clusters;
+      e = launch_gemm1_pair(tm_a, tm_a32, tm_w13, g1, 2 * clusters, s);
+    } else {
+      const int units = w.nt_cap * kIB;
+      e = launch_gemm1(tm_a, tm_a32, tm_w13, g1, units < num_sms ? units : num_sms, s);
+    }
+    if (e != cudaSuccess) return KF_ERR_CUDA;
   }
 
   Gemm2Args g2;
   g2.meta = meta;
-  g2.tile_expert = g1.tile_expert;
-  g2.tile_row0 = g1.tile_row0;
-  g2.tile_rows = g1.tile_rows;
+  g2.tile_expert = t_exp;
+  g2.tile_row0 = t_row0;
+  g2.tile_rows = t_rows;
   g2.c_scale = g1.c_scale;
   g2.w2_scale = w2_scale;
   g2.slot_weight = ws_ptr<float>(ws, w.slot_weight);
   g2.y = ws_ptr<float>(ws, w.y);
   g2.p_cap = w.p_cap;
   g2.status = status;
-  const int units2 = w.nt_cap * (kH / 256);
   {
     ProfScope ps(KF_KERNEL_GEMM2, s);
-    if (launch_gemm2(tm_chi, tm_clo, tm_chi32, tm_clo32, tm_w2, g2, units2 < num_sms ? units2 : num_sms, s) != cudaSuccess)
-      return KF_ERR_CUDA;
+    cudaError_t e;
+    const int units = w.nt_cap * (kH / 256);
+    if (pair) {
+      const int clusters = units < pair_clusters ? units : pair_clusters;
+      e = launch_gemm2_pair(tm_chi, tm_clo, tm_chi32, tm_clo32, tm_w2_half, g2, 2 * clusters, s);
+    } else {
+      e = launch_gemm2(tm_chi, tm_clo, tm_chi32, tm_clo32, tm_w2, g2, units < num_sms ? units : num_sms, s);
+    }
+    if (e != cudaSuccess) return KF_ERR_CUDA;
   }
 
   {
@@ -242,8 +278,10 @@ int run_experts(const Workspace& w, void* ws, const int32_t* topk_idx, const flo
 Workspace plan_workspace(int32_t T, int32_t E) {
   Workspace w{};
   const int64_t pairs_max = static_cast<int64_t>(T) * (E < kTopK ? E : kTopK);
-  const int64_t rows = align_up(static_cast<size_t>(pairs_max + static_cast<int64_t>(E) * (kBlk - 1)), kBlk);
-  w.p_cap = static_cast<int32_t>(rows > 0 ? rows : kBlk);
+  // + one tile of slack: the last 256-row pair tile may extend 128 rows past the last segment
+  const int64_t rows =
+      align_up(static_cast<size_t>(pairs_max + static_cast<int64_t>(E) * (kBlk - 1)), kBlk) + kBlk;
+  w.p_cap = static_cast<int32_t>(rows);
   w.nt_cap = w.p_cap / kBlk;
   w.nchunk = (T + kChunkTokens - 1) / kChunkTokens;
   size_t off = 0;
@@ -264,6 +302,9 @@ Workspace plan_workspace(int32_t T, int32_t E) {
   w.tile_expert = take(static_cast<size_t>(w.nt_cap) * 4);
   w.tile_row0 = take(static_cast<size_t>(w.nt_cap) * 4);
   w.tile_rows = take(static_cast<size_t>(w.nt_cap) * 4);
+  w.ptile_expert = take(static_cast<size_t>(w.nt_cap) * 4);
+  w.ptile_row0 = take(static_cast<size_t>(w.nt_cap) * 4);
+  w.ptile_rows = take(static_cast<size_t>(w.nt_cap) * 4);
   w.slot_token = take(pc * 4);
   w.slot_weight = take(pc * 4);
   w.a_rows = take(pc * kH);
@@ -336,8 +377,8 @@ int kf_moe_forward(const float* routing_logits, const void* routing_bias, const 
     return KF_ERR_INVALID_ARGUMENT;
   const Workspace w = plan_workspace(T, E);
   if (workspace_bytes < w.total) return KF_ERR_WORKSPACE_TOO_SMALL;
-  int sms = 0;
-  rc = ensure_device(&sms);
+  int sms = 0, pair_clusters = 0;
+  rc = ensure_device(&sms, &pair_clusters);
   if (rc != KF_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(ws_ptr<int>(workspace, w.status), 0, sizeof(int), s) != cudaSuccess) return KF_ERR_CUDA;
@@ -351,7 +392,7 @@ int kf_moe_forward(const float* routing_logits, const void* routing_bias, const 
   }
   return run_experts(w, workspace, topk_idx, topk_w, hidden_states, hidden_states_scale, gemm1_weights,
                      gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, T, E, local_expert_offset, output, 0,
-                     sms, s);
+                     sms, pair_clusters, s);
 }
 
 int kf_moe_experts(const int32_t* topk_idx, const float* topk_weight, const void* hidden_states,
@@ -371,8 +412,8 @@ int kf_moe_experts(const int32_t* topk_idx, const float* topk_weight, const void
     return KF_ERR_INVALID_ARGUMENT;
   const Workspace w = plan_workspace(T, E);
   if (workspace_bytes < w.total) return KF_ERR_WORKSPACE_TOO_SMALL;
-  int sms = 0;
-  rc = ensure_device(&sms);
+  int sms = 0, pair_clusters = 0;
+  rc = ensure_device(&sms, &pair_clusters);
   if (rc != KF_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int* status = ws_ptr<int>(workspace, w.status);
@@ -385,7 +426,7 @@ int kf_moe_experts(const int32_t* topk_idx, const float* topk_weight, const void
   }
   return run_experts(w, workspace, topk_idx, topk_weight, hidden_states, hidden_states_scale, gemm1_weights,
                      gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, T, E, local_expert_offset, output,
-                     output_fp32 ? 1 : 0, sms, s);
+                     output_fp32 ? 1 : 0, sms, pair_clusters, s);
 }
 
 int kf_moe_profile_begin(void) {

@@ -189,11 +189,15 @@ __device__ __forceinline__ int popc4(uint4 m) { return __popc(m.x) + __popc(m.y)
 
 // One block; thread e owns local expert e.  Running counts over chunks give each
 // chunk's base inside the expert's segment (stable: chunk order = token order).
+// Each expert's rows are one 128-aligned segment; it is cut into 128-row tiles
+// (single-CTA GEMMs) and 256-row pair tiles (CTA-pair GEMMs).
 __global__ void __launch_bounds__(kMaxLocalExperts) permute_scan_kernel(
     const uint4* __restrict__ chunk_masks, int nchunk, int E, Meta* __restrict__ meta,
     int32_t* __restrict__ chunk_base, int32_t* __restrict__ tile_expert, int32_t* __restrict__ tile_row0,
-    int32_t* __restrict__ tile_rows, int nt_cap, int* status) {
+    int32_t* __restrict__ tile_rows, int32_t* __restrict__ ptile_expert, int32_t* __restrict__ ptile_row0,
+    int32_t* __restrict__ ptile_rows, int nt_cap, int* status) {
   __shared__ int32_t tiles_scan[kMaxLocalExperts];
+  __shared__ int32_t ptiles_scan[kMaxLocalExperts];
   __shared__ int32_t pairs_scan[kMaxLocalExperts];
   const int e = threadIdx.x;
   int run = 0;
@@ -219,20 +223,26 @@ __global__ void __launch_bounds__(kMaxLocalExperts) permute_scan_kernel(
     }
   }
   const int ntiles = (run + kBlk - 1) / kBlk;
+  const int nptiles = (run + 2 * kBlk - 1) / (2 * kBlk);
   tiles_scan[e] = ntiles;
+  ptiles_scan[e] = nptiles;
   pairs_scan[e] = run;
   __syncthreads();
-  // inclusive Hillis-Steele scan over 256 entries
+  // inclusive Hillis-Steele scans over 256 entries
   for (int off = 1; off < kMaxLocalExperts; off <<= 1) {
     const int a = (e >= off) ? tiles_scan[e - off] : 0;
     const int b = (e >= off) ? pairs_scan[e - off] : 0;
+    const int c = (e >= off) ? ptiles_scan[e - off] : 0;
     __syncthreads();
     tiles_scan[e] += a;
     pairs_scan[e] += b;
+    ptiles_scan[e] += c;
     __syncthreads();
   }
   const int tstart = tiles_scan[e] - ntiles;
+  const int pstart = ptiles_scan[e] - nptiles;
   const int total_tiles = tiles_scan[kMaxLocalExperts - 1];
+  const int total_ptiles = ptiles_scan[kMaxLocalExperts - 1];
   if (e < E) {
     meta->expert_count[e] = run;
     meta->expert_pad_start[e] = tstart * kBlk;
@@ -243,12 +253,23 @@ __global__ void __launch_bounds__(kMaxLocalExperts) permute_scan_kernel(
         break;
       }
       tile_expert[ti] = e;
-      tile_row0[ti] = (tstart + i) * kBlk;
+      tile_row0[ti] = ti * kBlk;
       tile_rows[ti] = min(kBlk, run - i * kBlk);
+    }
+    for (int i = 0; i < nptiles; ++i) {
+      const int pi = pstart + i;
+      if (pi >= nt_cap) {
+        record_error(status, KF_STATUS_SLOT_OVERFLOW);
+        break;
+      }
+      ptile_expert[pi] = e;
+      ptile_row0[pi] = tstart * kBlk + i * 2 * kBlk;
+      ptile_rows[pi] = min(2 * kBlk, run - i * 2 * kBlk);
     }
   }
   if (e == 0) {
     meta->num_tiles = min(total_tiles, nt_cap);
+    meta->num_ptiles = min(total_ptiles, nt_cap);
     meta->num_pairs = pairs_scan[kMaxLocalExperts - 1];
   }
 }
@@ -401,10 +422,11 @@ cudaError_t launch_masks_from_topk(const int32_t* topk_idx, int T, int E, int of
 }
 
 cudaError_t launch_permute_scan(const uint4* chunk_masks, int nchunk, int E, Meta* meta, int32_t* chunk_base,
-                                int32_t* tile_expert, int32_t* tile_row0, int32_t* tile_rows, int nt_cap,
-                                int* status, cudaStream_t s) {
+                                int32_t* tile_expert, int32_t* tile_row0, int32_t* tile_rows, int32_t* ptile_expert,
+                                int32_t* ptile_row0, int32_t* ptile_rows, int nt_cap, int* status, cudaStream_t s) {
   permute_scan_kernel<<<1, kMaxLocalExperts, 0, s>>>(chunk_masks, nchunk, E, meta, chunk_base, tile_expert,
-                                                     tile_row0, tile_rows, nt_cap, status);
+                                                     tile_row0, tile_rows, ptile_expert, ptile_row0, ptile_rows,
+                                                     nt_cap, status);
   return cudaGetLastError();
 }
 

@@ -81,3 +81,16 @@ def test_python_kernel_refuses_cpu_tensors():
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         B.kernel(ti.routing_logits, ti.routing_bias, ti.hidden_states, ti.hidden_states_scale,
                  wb.gemm1_weights, wb.gemm1_weights_scale, wb.gemm2_weights, wb.gemm2_weights_scale, 0, 2.5)
+
+
+def test_noalloc_static_scratch_covers_its_limits():
+    """The static scratch of the allocation-free entry point holds the workspace
+    of its largest accepted call (checked on the host, so layout changes that
+    outgrow it fail here rather than on a GPU)."""
+    text = open(os.path.join(ROOT, "include", "kf_moe.h")).read()
+    size = re.search(r"#define KF_MOE_NOALLOC_SCRATCH_BYTES \((\d+)u << (\d+)\)", text)
+    max_t = int(re.search(r"#define KF_MOE_NOALLOC_MAX_TOKENS (\d+)", text).group(1))
+    max_e = int(re.search(r"#define KF_MOE_NOALLOC_MAX_LOCAL_EXPERTS (\d+)", text).group(1))
+    scratch = int(size.group(1)) << int(size.group(2))
+    lib = B.library()
+    assert all(lib.kf_moe_workspace_bytes(t, e) <= scratch for t in (1, max_t) for e in (1, max_e))
