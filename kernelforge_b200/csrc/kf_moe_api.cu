@@ -64,10 +64,14 @@ struct ProfScope {
   }
 };
 
-// KF_MOE_GEMM=1sm selects the single-CTA GEMMs (for comparison); the default is the CTA-pair GEMMs.
+// KF_MOE_GEMM=pair selects the CTA-pair (cta_group::2) GEMMs; the default is the
+// single-CTA GEMMs.  The pair kernels move a third fewer bytes per SM, but the
+// per-K-chunk promotion handshake then crosses SMs (commit multicast to the peer,
+// remote arrival back) and, with two TMEM partial buffers, that latency is not
+// hidden: measured ~1.7x slower on B200, so they are opt-in.
 bool pair_gemms_requested() {
   const char* v = getenv("KF_MOE_GEMM");
-  return !(v && strcmp(v, "1sm") == 0);
+  return v && strcmp(v, "pair") == 0;
 }
 
 int ensure_device(int* num_sms, int* pair_clusters = nullptr) {
@@ -88,6 +92,9 @@ int ensure_device(int* num_sms, int* pair_clusters = nullptr) {
       d.status = KF_OK;
       d.pair_clusters = pair_gemms_requested() ? gemm_pair_max_clusters() : 0;
     }
+    if (getenv("KF_MOE_DEBUG"))
+      fprintf(stderr, "kf_moe: device %d sms=%d pair_clusters=%d status=%d\n", dev, d.num_sms, d.pair_clusters,
+              d.status);
     if (!g_encode && d.status == KF_OK) {
       void* fn = nullptr;
       cudaDriverEntryPointQueryResult q;

@@ -1,5 +1,5 @@
-"""Both GEMM implementations -- CTA-pair (cta_group::2, default) and single-CTA
-(KF_MOE_GEMM=1sm) -- against the fp32 reference, each in a fresh process (the
+"""Both GEMM implementations -- single-CTA (default) and CTA-pair (cta_group::2,
+KF_MOE_GEMM=pair) -- against the fp32 reference, each in a fresh process (the
 path is chosen once per process)."""
 import os
 import subprocess
@@ -38,11 +38,11 @@ sys.exit(1 if bad else 0)
 """ % ROOT
 
 
-@pytest.mark.parametrize("path", ["pair", "1sm"])
+@pytest.mark.parametrize("path", ["1sm", "pair"])
 def test_gemm_path_parity(path):
     env = dict(os.environ)
-    if path == "1sm":
-        env["KF_MOE_GEMM"] = "1sm"
+    if path == "pair":
+        env["KF_MOE_GEMM"] = "pair"
     else:
         env.pop("KF_MOE_GEMM", None)
     r = subprocess.run([sys.executable, "-c", SCRIPT], env=env, capture_output=True, text=True, timeout=600)
