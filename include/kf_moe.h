@@ -122,7 +122,7 @@ int kf_moe_read_status(void* workspace, int32_t* status, void* stream);
 /* Limits of kf_moe_forward_noalloc and the size of its static scratch array. */
 #define KF_MOE_NOALLOC_MAX_TOKENS 16
 #define KF_MOE_NOALLOC_MAX_LOCAL_EXPERTS 32
-#define KF_MOE_NOALLOC_SCRATCH_BYTES (168u << 20) /* 168 MiB */
+#define KF_MOE_NOALLOC_SCRATCH_BYTES (176u << 20) /* 176 MiB */
 
 /*
  * kf_moe_forward for callers that cannot allocate device memory.  This entry
@@ -167,7 +167,8 @@ int kf_moe_forward_noalloc(const float* routing_logits, const void* routing_bias
 #define KF_KERNEL_GEMM1 5
 #define KF_KERNEL_GEMM2 6
 #define KF_KERNEL_REDUCE 7
-#define KF_KERNEL_COUNT 8
+#define KF_KERNEL_FRONT_SMALL 8
+#define KF_KERNEL_COUNT 9
 
 /*
  * Profiling.  Between kf_moe_profile_begin() and kf_moe_profile_end(), every
@@ -179,7 +180,8 @@ int kf_moe_forward_noalloc(const float* routing_logits, const void* routing_bias
 int kf_moe_profile_begin(void);
 int kf_moe_profile_end(float* total_ms, int32_t* launches, int32_t n);
 
-/* Diagnostics: number of kernels one kf_moe_forward launches. */
+/* Diagnostics: number of kernels one kf_moe_forward launches for T > 128 tokens
+ * (calls of at most 128 tokens run a single-block front end: 4 kernels). */
 int32_t kf_moe_launches_per_forward(void);
 
 /* Human-readable text for a KF_ERR_* code. */

@@ -33,12 +33,14 @@ struct Meta {
 // Offsets (bytes) of every scratch array inside the caller's workspace.
 struct Workspace {
   size_t status, meta, topk_idx, topk_w, token_slot, chunk_masks, chunk_base;
-  size_t tile_expert, tile_row0, tile_rows, ptile_expert, ptile_row0, ptile_rows, slot_token, slot_weight;
-  size_t a_rows, a_scale, c_hi, c_lo, c_scale, y;
+  size_t tile_expert, tile_row0, tile_rows, ptile_expert, ptile_row0, ptile_rows, slot_token, slot_weight, slot_pair;
+  size_t a_rows, a_scale, c_hi, c_lo, c_scale, y, partial, fix_count;
   size_t total;
   int32_t p_cap;    // capacity in permuted rows (multiple of 128)
   int32_t nt_cap;   // capacity in row tiles
   int32_t nchunk;   // routing/permute chunks of 128 tokens
+  int32_t ksplit1;  // split-K factors of GEMM1 / GEMM2 (1 = no split)
+  int32_t ksplit2;
 };
 
 Workspace plan_workspace(int32_t T, int32_t E);
@@ -58,8 +60,16 @@ cudaError_t launch_permute_scan(const uint4* chunk_masks, int nchunk, int E, Met
                                 int32_t* ptile_row0, int32_t* ptile_rows, int nt_cap, int* status, cudaStream_t s);
 cudaError_t launch_permute_assign(const int32_t* topk_idx, const float* topk_w, const uint4* chunk_masks,
                                   const int32_t* chunk_base, const Meta* meta, int T, int E, int offset, int p_cap,
-                                  int32_t* token_slot, int32_t* slot_token, float* slot_weight, int* status,
-                                  cudaStream_t s);
+                                  int32_t* token_slot, int32_t* slot_token, float* slot_weight, int32_t* slot_pair,
+                                  int* status, cudaStream_t s);
+// Single-block front end for T <= kChunkTokens: routing (logits != nullptr) or the
+// caller's routing (topk_in), tile lists, slots and the row gather.
+cudaError_t launch_front_small(const float* logits, const void* bias, float rsf, const int32_t* topk_in,
+                               const float* topk_w_in, const uint8_t* hidden, const float* hidden_scale, int T, int E,
+                               int offset, int p_cap, Meta* meta, int32_t* tile_expert, int32_t* tile_row0,
+                               int32_t* tile_rows, int32_t* ptile_expert, int32_t* ptile_row0, int32_t* ptile_rows,
+                               int32_t* token_slot, int32_t* slot_token, float* slot_weight, int32_t* slot_pair,
+                               uint8_t* a_rows, float* a_scale, int* status, cudaStream_t s);
 cudaError_t launch_gather_rows(const Meta* meta, const int32_t* tile_rows, const int32_t* slot_token,
                                const uint8_t* hidden, const float* hidden_scale, int T, int p_cap, uint8_t* a_rows,
                                float* a_scale, int grid, cudaStream_t s);
@@ -80,6 +90,16 @@ struct Gemm1Args {
   float* c_scale;          // [16][p_cap]
   int32_t p_cap;
   int* status;
+  // Split-K (single-CTA kernel only): ksplit CTAs share a (tile, column block),
+  // each over 56/ksplit K chunks; their fp32 partial sums go to `partial`
+  // ([ksplit][max_pairs][4096], indexed by the pair id slot_pair[row]) and the
+  // last CTA to finish (counted in fix_count) sums them in split order and runs
+  // the epilogue.
+  int32_t ksplit;
+  int32_t max_pairs;
+  const int32_t* slot_pair;
+  float* partial;
+  int* fix_count;
 };
 
 struct Gemm2Args {
@@ -93,6 +113,11 @@ struct Gemm2Args {
   float* y;                 // [p_cap][7168]
   int32_t p_cap;
   int* status;
+  int32_t ksplit;           // as in Gemm1Args; partial is [ksplit][max_pairs][7168]
+  int32_t max_pairs;
+  const int32_t* slot_pair;
+  float* partial;
+  int* fix_count;
 };
 
 cudaError_t launch_gemm1(const CUtensorMap& tm_a, const CUtensorMap& tm_a32, const CUtensorMap& tm_w13,

@@ -7,6 +7,7 @@
 
 #include <cstdio>
 #include <cstdlib>
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -19,6 +20,7 @@ namespace kf {
 namespace {
 
 constexpr size_t kAlign = 256;
+constexpr int kSplitKMaxT = 64;  // calls of at most this many tokens split the GEMMs' K loop
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 struct DeviceInfo {
@@ -165,14 +167,18 @@ int check_common(int32_t T, int32_t E, int32_t offset) {
   return KF_OK;
 }
 
-// Permutation, both grouped GEMMs and the reduce, from chunk masks already in the workspace.
+// Calls of at most this many tokens run the single-block front end.
+constexpr int kSmallT = kChunkTokens;
+
+// Permutation (unless the single-block front end already did it), both grouped
+// GEMMs and the reduce, from chunk masks already in the workspace.
 int run_experts(const Workspace& w, void* ws, const int32_t* topk_idx, const float* topk_w, const void* hidden,
                 const float* hidden_scale, const void* w13, const float* w13_scale, const void* w2,
                 const float* w2_scale, int T, int E, int offset, void* out, int out_fp32, int num_sms,
-                int pair_clusters, cudaStream_t s) {
+                int pair_clusters, bool front_done, cudaStream_t s) {
   int* status = ws_ptr<int>(ws, w.status);
   Meta* meta = ws_ptr<Meta>(ws, w.meta);
-  {
+  if (!front_done) {
     ProfScope ps(KF_KERNEL_PERMUTE_SCAN, s);
     if (launch_permute_scan(ws_ptr<uint4>(ws, w.chunk_masks), w.nchunk, E, meta, ws_ptr<int32_t>(ws, w.chunk_base),
                             ws_ptr<int32_t>(ws, w.tile_expert), ws_ptr<int32_t>(ws, w.tile_row0),
@@ -181,15 +187,15 @@ int run_experts(const Workspace& w, void* ws, const int32_t* topk_idx, const flo
                             s) != cudaSuccess)
       return KF_ERR_CUDA;
   }
-  {
+  if (!front_done) {
     ProfScope ps(KF_KERNEL_PERMUTE_ASSIGN, s);
     if (launch_permute_assign(topk_idx, topk_w, ws_ptr<uint4>(ws, w.chunk_masks), ws_ptr<int32_t>(ws, w.chunk_base),
                               meta, T, E, offset, w.p_cap, ws_ptr<int32_t>(ws, w.token_slot),
-                              ws_ptr<int32_t>(ws, w.slot_token), ws_ptr<float>(ws, w.slot_weight), status,
-                              s) != cudaSuccess)
+                              ws_ptr<int32_t>(ws, w.slot_token), ws_ptr<float>(ws, w.slot_weight),
+                              ws_ptr<int32_t>(ws, w.slot_pair), status, s) != cudaSuccess)
       return KF_ERR_CUDA;
   }
-  {
+  if (!front_done) {
     ProfScope ps(KF_KERNEL_GATHER_ROWS, s);
     if (launch_gather_rows(meta, ws_ptr<int32_t>(ws, w.tile_rows), ws_ptr<int32_t>(ws, w.slot_token),
                            static_cast<const uint8_t*>(hidden), hidden_scale, T, w.p_cap,
@@ -233,6 +239,14 @@ int run_experts(const Workspace& w, void* ws, const int32_t* topk_idx, const flo
   g1.c_scale = ws_ptr<float>(ws, w.c_scale);
   g1.p_cap = w.p_cap;
   g1.status = status;
+  g1.ksplit = pair ? 1 : w.ksplit1;
+  g1.max_pairs = T * kTopK;
+  g1.slot_pair = ws_ptr<int32_t>(ws, w.slot_pair);
+  g1.partial = ws_ptr<float>(ws, w.partial);
+  g1.fix_count = ws_ptr<int>(ws, w.fix_count);
+  if ((g1.ksplit > 1 || (!pair && w.ksplit2 > 1)) &&
+      cudaMemsetAsync(g1.fix_count, 0, static_cast<size_t>(w.nt_cap) * (kH / 256) * 4, s) != cudaSuccess)
+    return KF_ERR_CUDA;
   {
     ProfScope ps(KF_KERNEL_GEMM1, s);
     cudaError_t e;
@@ -241,7 +255,7 @@ int run_experts(const Workspace& w, void* ws, const int32_t* topk_idx, const flo
       const int clusters = units < pair_clusters ? units : pair_clusters;
       e = launch_gemm1_pair(tm_a, tm_a32, tm_w13, g1, 2 * clusters, s);
     } else {
-      const int units = w.nt_cap * kIB;
+      const int units = w.nt_cap * kIB * g1.ksplit;
       e = launch_gemm1(tm_a, tm_a32, tm_w13, g1, units < num_sms ? units : num_sms, s);
     }
     if (e != cudaSuccess) return KF_ERR_CUDA;
@@ -258,6 +272,11 @@ int run_experts(const Workspace& w, void* ws, const int32_t* topk_idx, const flo
   g2.y = ws_ptr<float>(ws, w.y);
   g2.p_cap = w.p_cap;
   g2.status = status;
+  g2.ksplit = pair ? 1 : w.ksplit2;
+  g2.max_pairs = T * kTopK;
+  g2.slot_pair = g1.slot_pair;
+  g2.partial = g1.partial;
+  g2.fix_count = g1.fix_count;
   {
     ProfScope ps(KF_KERNEL_GEMM2, s);
     cudaError_t e;
@@ -266,7 +285,8 @@ int run_experts(const Workspace& w, void* ws, const int32_t* topk_idx, const flo
       const int clusters = units < pair_clusters ? units : pair_clusters;
       e = launch_gemm2_pair(tm_chi, tm_clo, tm_chi32, tm_clo32, tm_w2_half, g2, 2 * clusters, s);
     } else {
-      e = launch_gemm2(tm_chi, tm_clo, tm_chi32, tm_clo32, tm_w2, g2, units < num_sms ? units : num_sms, s);
+      const int units_k = units * g2.ksplit;
+      e = launch_gemm2(tm_chi, tm_clo, tm_chi32, tm_clo32, tm_w2, g2, units_k < num_sms ? units_k : num_sms, s);
     }
     if (e != cudaSuccess) return KF_ERR_CUDA;
   }
@@ -278,6 +298,22 @@ int run_experts(const Workspace& w, void* ws, const int32_t* topk_idx, const flo
       return KF_ERR_CUDA;
   }
   return KF_OK;
+}
+
+int run_front_small(const Workspace& w, void* ws, const float* logits, const void* bias, float rsf,
+                    const int32_t* topk_in, const float* topk_w_in, const void* hidden, const float* hidden_scale,
+                    int T, int E, int offset, cudaStream_t s) {
+  ProfScope ps(KF_KERNEL_FRONT_SMALL, s);
+  return launch_front_small(logits, bias, rsf, topk_in, topk_w_in, static_cast<const uint8_t*>(hidden), hidden_scale,
+                            T, E, offset, w.p_cap, ws_ptr<Meta>(ws, w.meta), ws_ptr<int32_t>(ws, w.tile_expert),
+                            ws_ptr<int32_t>(ws, w.tile_row0), ws_ptr<int32_t>(ws, w.tile_rows),
+                            ws_ptr<int32_t>(ws, w.ptile_expert), ws_ptr<int32_t>(ws, w.ptile_row0),
+                            ws_ptr<int32_t>(ws, w.ptile_rows), ws_ptr<int32_t>(ws, w.token_slot),
+                            ws_ptr<int32_t>(ws, w.slot_token), ws_ptr<float>(ws, w.slot_weight),
+                            ws_ptr<int32_t>(ws, w.slot_pair), ws_ptr<uint8_t>(ws, w.a_rows),
+                            ws_ptr<float>(ws, w.a_scale), ws_ptr<int>(ws, w.status), s) == cudaSuccess
+             ? KF_OK
+             : KF_ERR_CUDA;
 }
 
 }  // namespace
@@ -314,12 +350,21 @@ Workspace plan_workspace(int32_t T, int32_t E) {
   w.ptile_rows = take(static_cast<size_t>(w.nt_cap) * 4);
   w.slot_token = take(pc * 4);
   w.slot_weight = take(pc * 4);
+  w.slot_pair = take(pc * 4);
   w.a_rows = take(pc * kH);
   w.a_scale = take(pc * kHB * 4);
   w.c_hi = take(pc * kI);
   w.c_lo = take(pc * kI);
   w.c_scale = take(pc * kIB * 4);
   w.y = take(pc * kH * 4);
+  // split-K for decode-sized calls: fewer tiles than SMs otherwise leave most SMs
+  // idle and quantise the weight stream into ~2 waves
+  w.ksplit1 = T <= kSplitKMaxT ? 4 : 1;
+  w.ksplit2 = T <= kSplitKMaxT ? 2 : 1;
+  const size_t max_pairs = static_cast<size_t>(T) * kTopK;
+  const size_t split_cols = std::max(static_cast<size_t>(w.ksplit1) * kI * 2, static_cast<size_t>(w.ksplit2) * kH);
+  w.partial = take(w.ksplit1 > 1 || w.ksplit2 > 1 ? split_cols * max_pairs * 4 : 0);
+  w.fix_count = take(static_cast<size_t>(w.nt_cap) * (kH / 256) * 4);
   w.total = off;
   return w;
 }
@@ -391,7 +436,12 @@ int kf_moe_forward(const float* routing_logits, const void* routing_bias, const 
   if (cudaMemsetAsync(ws_ptr<int>(workspace, w.status), 0, sizeof(int), s) != cudaSuccess) return KF_ERR_CUDA;
   int32_t* topk_idx = ws_ptr<int32_t>(workspace, w.topk_idx);
   float* topk_w = ws_ptr<float>(workspace, w.topk_w);
-  {
+  const bool small = T <= kSmallT;
+  if (small) {
+    rc = run_front_small(w, workspace, routing_logits, routing_bias, routed_scaling_factor, nullptr, nullptr,
+                         hidden_states, hidden_states_scale, T, E, local_expert_offset, s);
+    if (rc != KF_OK) return rc;
+  } else {
     ProfScope ps(KF_KERNEL_ROUTE, s);
     if (launch_route(routing_logits, routing_bias, T, routed_scaling_factor, topk_idx, topk_w, E,
                      local_expert_offset, ws_ptr<uint4>(workspace, w.chunk_masks), s) != cudaSuccess)
@@ -399,7 +449,7 @@ int kf_moe_forward(const float* routing_logits, const void* routing_bias, const 
   }
   return run_experts(w, workspace, topk_idx, topk_w, hidden_states, hidden_states_scale, gemm1_weights,
                      gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, T, E, local_expert_offset, output, 0,
-                     sms, pair_clusters, s);
+                     sms, pair_clusters, small, s);
 }
 
 int kf_moe_experts(const int32_t* topk_idx, const float* topk_weight, const void* hidden_states,
@@ -425,7 +475,12 @@ int kf_moe_experts(const int32_t* topk_idx, const float* topk_weight, const void
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int* status = ws_ptr<int>(workspace, w.status);
   if (cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess) return KF_ERR_CUDA;
-  {
+  const bool small = T <= kSmallT;
+  if (small) {
+    rc = run_front_small(w, workspace, nullptr, nullptr, 0.f, topk_idx, topk_weight, hidden_states,
+                         hidden_states_scale, T, E, local_expert_offset, s);
+    if (rc != KF_OK) return rc;
+  } else {
     ProfScope ps(KF_KERNEL_MASKS, s);
     if (launch_masks_from_topk(topk_idx, T, E, local_expert_offset, ws_ptr<uint4>(workspace, w.chunk_masks),
                                status, s) != cudaSuccess)
@@ -433,7 +488,7 @@ int kf_moe_experts(const int32_t* topk_idx, const float* topk_weight, const void
   }
   return run_experts(w, workspace, topk_idx, topk_weight, hidden_states, hidden_states_scale, gemm1_weights,
                      gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, T, E, local_expert_offset, output,
-                     output_fp32 ? 1 : 0, sms, pair_clusters, s);
+                     output_fp32 ? 1 : 0, sms, pair_clusters, small, s);
 }
 
 int kf_moe_profile_begin(void) {

@@ -25,9 +25,127 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
   return v > bv || (v == bv && i < bi);
 }
 
-// One warp routes one token.  Lane l owns experts [8l, 8l+8); group g = lanes [4g, 4g+4).
-// With chunk_masks (zeroed beforehand), the token's bit is set in the mask of
-// each selected local expert for the token's chunk of 128.
+// Routes one token with one warp.  Lane l owns experts [8l, 8l+8); group g is
+// lanes [4g, 4g+4).  On return lane k < 8 holds the k-th selected expert (in
+// descending biased-score order, ties to the lower id) and its weight.
+__device__ __forceinline__ void route_one_token(const float* __restrict__ logits_row, const float (&b)[8], float rsf,
+                                                int lane, int& e_out, float& w_out) {
+  const float4* lp = reinterpret_cast<const float4*>(logits_row + lane * 8);
+  const float4 x0 = lp[0], x1 = lp[1];
+  const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+  float s[8], sb[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    s[j] = 1.0f / (1.0f + expf(-x[j]));
+    sb[j] = s[j] + b[j];
+  }
+  // group score: sum of the two largest biased scores of the group's 32 experts
+  float m1 = -INFINITY, m2 = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (sb[j] > m1) {
+      m2 = m1;
+      m1 = sb[j];
+    } else if (sb[j] > m2) {
+      m2 = sb[j];
+    }
+  }
+#pragma unroll
+  for (int off = 1; off <= 2; off <<= 1) {
+    const float o1 = __shfl_xor_sync(0xffffffffu, m1, off);
+    const float o2 = __shfl_xor_sync(0xffffffffu, m2, off);
+    const float n2 = fmaxf(fminf(m1, o1), fmaxf(m2, o2));
+    m1 = fmaxf(m1, o1);
+    m2 = n2;
+  }
+  const float gscore = m1 + m2;
+  float gs[8];
+#pragma unroll
+  for (int g = 0; g < 8; ++g) gs[g] = __shfl_sync(0xffffffffu, gscore, 4 * g);
+  // keep the 4 best groups (ties: lower group index wins)
+  const int my_group = lane >> 2;
+  int rank = 0;
+#pragma unroll
+  for (int g = 0; g < 8; ++g) rank += better(gs[g], g, gs[my_group], my_group) ? 1 : 0;
+  uint32_t avail = (rank < 4) ? 0xFFu : 0u;
+  // top-8 over the kept experts by biased score (ties: lower expert id wins)
+  int sel[8];
+  float sel_s[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if ((avail >> j) & 1u) {
+        if (better(sb[j], lane * 8 + j, bv, bi)) {
+          bv = sb[j];
+          bi = lane * 8 + j;
+        }
+      }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      if (better(ov, oi, bv, bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    sel[k] = bi;
+    const int owner = bi >> 3, jj = bi & 7;
+    float mine = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j == jj) mine = s[j];
+    sel_s[k] = __shfl_sync(0xffffffffu, mine, owner);
+    if (lane == owner) avail &= ~(1u << jj);
+  }
+  // normalise the un-biased scores in ascending expert order, then scale
+  float sum = 0.f;
+  {
+    int order[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      int r = 0;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) r += (sel[q] < sel[k]) ? 1 : 0;
+      order[k] = r;
+    }
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      float v = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (order[k] == r) v = sel_s[k];
+      sum += v;
+    }
+  }
+  const float denom = sum + 1e-20f;
+  e_out = 0;
+  w_out = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    if (k == lane) {
+      e_out = sel[k];
+      w_out = (sel_s[k] / denom) * rsf;
+    }
+}
+
+__device__ __forceinline__ void load_bias8(const __nv_bfloat16* __restrict__ bias, int lane, float (&b)[8]) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(bias + lane * 8);
+  const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = __bfloat1622float2(p[j]);
+    b[2 * j] = f.x;
+    b[2 * j + 1] = f.y;
+  }
+}
+
+// One warp routes one token.  With chunk_masks (zeroed beforehand), the token's
+// bit is set in the mask of each selected local expert for the token's chunk of 128.
 __global__ void __launch_bounds__(kRouteThreads) route_kernel(const float* __restrict__ logits,
                                                               const __nv_bfloat16* __restrict__ bias, int T,
                                                               float rsf, int32_t* __restrict__ topk_idx,
@@ -37,127 +155,18 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const float* __res
   const int t = blockIdx.x * (kRouteThreads / 32) + (threadIdx.x >> 5);
   if (t >= T) return;
   float b[8];
-  {
-    const uint4 raw = *reinterpret_cast<const uint4*>(bias + lane * 8);
-    const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 f = __bfloat1622float2(p[j]);
-      b[2 * j] = f.x;
-      b[2 * j + 1] = f.y;
-    }
-  }
-  {
-    const float4* lp = reinterpret_cast<const float4*>(logits + static_cast<size_t>(t) * kEG + lane * 8);
-    const float4 x0 = lp[0], x1 = lp[1];
-    const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-    float s[8], sb[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      s[j] = 1.0f / (1.0f + expf(-x[j]));
-      sb[j] = s[j] + b[j];
-    }
-    // group score: sum of the two largest biased scores of the group's 32 experts
-    float m1 = -INFINITY, m2 = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if (sb[j] > m1) {
-        m2 = m1;
-        m1 = sb[j];
-      } else if (sb[j] > m2) {
-        m2 = sb[j];
-      }
-    }
-#pragma unroll
-    for (int off = 1; off <= 2; off <<= 1) {
-      const float o1 = __shfl_xor_sync(0xffffffffu, m1, off);
-      const float o2 = __shfl_xor_sync(0xffffffffu, m2, off);
-      const float n2 = fmaxf(fminf(m1, o1), fmaxf(m2, o2));
-      m1 = fmaxf(m1, o1);
-      m2 = n2;
-    }
-    const float gscore = m1 + m2;
-    float gs[8];
-#pragma unroll
-    for (int g = 0; g < 8; ++g) gs[g] = __shfl_sync(0xffffffffu, gscore, 4 * g);
-    // keep the 4 best groups (ties: lower group index wins)
-    const int my_group = lane >> 2;
-    int rank = 0;
-#pragma unroll
-    for (int g = 0; g < 8; ++g) rank += better(gs[g], g, gs[my_group], my_group) ? 1 : 0;
-    uint32_t avail = (rank < 4) ? 0xFFu : 0u;
-    // top-8 over the kept experts by biased score (ties: lower expert id wins)
-    int sel[8];
-    float sel_s[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if ((avail >> j) & 1u) {
-          if (better(sb[j], lane * 8 + j, bv, bi)) {
-            bv = sb[j];
-            bi = lane * 8 + j;
-          }
-        }
-      }
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-        if (better(ov, oi, bv, bi)) {
-          bv = ov;
-          bi = oi;
-        }
-      }
-      sel[k] = bi;
-      const int owner = bi >> 3, jj = bi & 7;
-      float mine = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (j == jj) mine = s[j];
-      sel_s[k] = __shfl_sync(0xffffffffu, mine, owner);
-      if (lane == owner) avail &= ~(1u << jj);
-    }
-    // normalise the un-biased scores in ascending expert order, then scale
-    float sum = 0.f;
-    {
-      int order[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        int r = 0;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) r += (sel[q] < sel[k]) ? 1 : 0;
-        order[k] = r;
-      }
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        float v = 0.f;
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-          if (order[k] == r) v = sel_s[k];
-        sum += v;
-      }
-    }
-    const float denom = sum + 1e-20f;
-    if (lane < 8) {
-      int e = 0;
-      float w = 0.f;
-#pragma unroll
-      for (int k = 0; k < 8; ++k)
-        if (k == lane) {
-          e = sel[k];
-          w = (sel_s[k] / denom) * rsf;
-        }
-      topk_idx[static_cast<size_t>(t) * kTopK + lane] = e;
-      topk_w[static_cast<size_t>(t) * kTopK + lane] = w;
-      if (chunk_masks) {
-        const int le = e - offset;
-        const int tl = t & (kChunkTokens - 1);
-        if (le >= 0 && le < E)
-          atomicOr(&chunk_masks[(static_cast<size_t>(t / kChunkTokens) * E + le) * 4 + (tl >> 5)], 1u << (tl & 31));
-      }
+  load_bias8(bias, lane, b);
+  int e;
+  float w;
+  route_one_token(logits + static_cast<size_t>(t) * kEG, b, rsf, lane, e, w);
+  if (lane < 8) {
+    topk_idx[static_cast<size_t>(t) * kTopK + lane] = e;
+    topk_w[static_cast<size_t>(t) * kTopK + lane] = w;
+    if (chunk_masks) {
+      const int le = e - offset;
+      const int tl = t & (kChunkTokens - 1);
+      if (le >= 0 && le < E)
+        atomicOr(&chunk_masks[(static_cast<size_t>(t / kChunkTokens) * E + le) * 4 + (tl >> 5)], 1u << (tl & 31));
     }
   }
 }
@@ -283,7 +292,7 @@ __global__ void __launch_bounds__(256) permute_assign_kernel(
     const int32_t* __restrict__ topk_idx, const float* __restrict__ topk_w, const uint4* __restrict__ chunk_masks,
     const int32_t* __restrict__ chunk_base, const Meta* __restrict__ meta, int T, int E, int offset, int p_cap,
     int32_t* __restrict__ token_slot, int32_t* __restrict__ slot_token, float* __restrict__ slot_weight,
-    int* status) {
+    int32_t* __restrict__ slot_pair, int* status) {
   __shared__ uint4 masks[kMaxLocalExperts];
   __shared__ int32_t base[kMaxLocalExperts];
   const int chunk = blockIdx.x;
@@ -315,6 +324,7 @@ __global__ void __launch_bounds__(256) permute_assign_kernel(
       } else {
         slot_token[slot] = t;
         slot_weight[slot] = topk_w[ti];
+        slot_pair[slot] = static_cast<int32_t>(ti);
       }
     }
     token_slot[ti] = slot;
@@ -346,6 +356,143 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const Meta* __restrict
     for (int j = 0; j < kH / 16 / 32; ++j) dst[lane + 32 * j] = v[j];
     for (int kb = lane; kb < kHB; kb += 32)
       a_scale[static_cast<size_t>(kb) * p_cap + r] = hidden_scale[static_cast<size_t>(kb) * T + t];
+  }
+}
+
+// Whole front end for a call of at most 128 tokens in ONE block (decode sizes,
+// where launch latency dominates): routing (or loading pre-routed ids), the
+// per-expert token masks, counts and the tile lists, stable slot assignment and
+// the gather of FP8 rows and scales -- the work of route / scan / assign /
+// gather_rows, with every intermediate in shared memory.  With at most 128
+// tokens an expert has at most 128 rows: one 128-row tile, one pair tile.
+constexpr int kFrontThreads = 1024;
+
+__global__ void __launch_bounds__(kFrontThreads) front_small_kernel(
+    const float* __restrict__ logits, const __nv_bfloat16* __restrict__ bias, float rsf,
+    const int32_t* __restrict__ topk_in, const float* __restrict__ topk_w_in, const uint8_t* __restrict__ hidden,
+    const float* __restrict__ hidden_scale, int T, int E, int offset, int p_cap, Meta* __restrict__ meta,
+    int32_t* __restrict__ tile_expert, int32_t* __restrict__ tile_row0, int32_t* __restrict__ tile_rows,
+    int32_t* __restrict__ ptile_expert, int32_t* __restrict__ ptile_row0, int32_t* __restrict__ ptile_rows,
+    int32_t* __restrict__ token_slot, int32_t* __restrict__ slot_token, float* __restrict__ slot_weight,
+    int32_t* __restrict__ slot_pair, uint8_t* __restrict__ a_rows, float* __restrict__ a_scale, int* status) {
+  __shared__ uint32_t masks[kMaxLocalExperts * 4];
+  __shared__ int32_t tk[kChunkTokens * kTopK];
+  __shared__ float tw[kChunkTokens * kTopK];
+  __shared__ int32_t pad_start[kMaxLocalExperts];
+  __shared__ int32_t warp_sums[kMaxLocalExperts / 32];
+  __shared__ int2 pairs[kChunkTokens * kTopK];
+  __shared__ int npairs, total_pairs;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int i = tid; i < kMaxLocalExperts * 4; i += kFrontThreads) masks[i] = 0u;
+  if (tid == 0) {
+    npairs = 0;
+    total_pairs = 0;
+  }
+  // routing, or the caller's routing
+  if (logits) {
+    float b[8];
+    load_bias8(bias, lane, b);
+    for (int t = warp; t < T; t += kFrontThreads / 32) {
+      int e;
+      float w;
+      route_one_token(logits + static_cast<size_t>(t) * kEG, b, rsf, lane, e, w);
+      if (lane < 8) {
+        tk[t * kTopK + lane] = e;
+        tw[t * kTopK + lane] = w;
+      }
+    }
+  } else {
+    for (int p = tid; p < T * kTopK; p += kFrontThreads) {
+      const int e = topk_in[p];
+      if (e >= kEG) record_error(status, KF_STATUS_BAD_EXPERT);
+      tk[p] = e;
+      tw[p] = topk_w_in[p];
+    }
+  }
+  __syncthreads();
+  for (int p = tid; p < T * kTopK; p += kFrontThreads) {
+    const int e = tk[p], le = e - offset, t = p >> 3;
+    if (e >= 0 && le >= 0 && le < E) atomicOr(&masks[le * 4 + (t >> 5)], 1u << (t & 31));
+  }
+  __syncthreads();
+  // counts, 128-aligned segments and the tile lists (an expert has 0 or 1 tile)
+  int cnt = 0, nt = 0;
+  if (tid < E) {
+    cnt = __popc(masks[tid * 4]) + __popc(masks[tid * 4 + 1]) + __popc(masks[tid * 4 + 2]) +
+          __popc(masks[tid * 4 + 3]);
+    nt = cnt > 0 ? 1 : 0;
+    atomicAdd(&total_pairs, cnt);
+  }
+  int incl = nt;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += n;
+  }
+  if (lane == 31 && warp < kMaxLocalExperts / 32) warp_sums[warp] = incl;
+  __syncthreads();
+  if (tid < kMaxLocalExperts) {
+    int base = 0, total = 0;
+    for (int w = 0; w < kMaxLocalExperts / 32; ++w) {
+      if (w < warp) base += warp_sums[w];
+      total += warp_sums[w];
+    }
+    const int tstart = base + incl - nt;
+    if (tid < E) {
+      pad_start[tid] = tstart * kBlk;
+      meta->expert_count[tid] = cnt;
+      meta->expert_pad_start[tid] = tstart * kBlk;
+      if (nt) {
+        tile_expert[tstart] = tid;
+        tile_row0[tstart] = tstart * kBlk;
+        tile_rows[tstart] = cnt;
+        ptile_expert[tstart] = tid;
+        ptile_row0[tstart] = tstart * kBlk;
+        ptile_rows[tstart] = cnt;
+      }
+    }
+    if (tid == 0) {
+      meta->num_tiles = total;
+      meta->num_ptiles = total;
+    }
+  }
+  __syncthreads();
+  if (tid == 0) meta->num_pairs = total_pairs;
+  // stable slots: segment start + earlier tokens of the same expert
+  for (int p = tid; p < T * kTopK; p += kFrontThreads) {
+    const int e = tk[p], le = e - offset, t = p >> 3;
+    int slot = -1;
+    if (e >= 0 && le >= 0 && le < E) {
+      const int w = t >> 5;
+      int r = __popc(masks[le * 4 + w] & ((1u << (t & 31)) - 1u));
+      for (int q = 0; q < w; ++q) r += __popc(masks[le * 4 + q]);
+      slot = pad_start[le] + r;
+      if (slot >= p_cap) {
+        record_error(status, KF_STATUS_SLOT_OVERFLOW);
+        slot = -1;
+      } else {
+        slot_token[slot] = t;
+        slot_weight[slot] = tw[p];
+        slot_pair[slot] = p;
+        pairs[atomicAdd(&npairs, 1)] = make_int2(t, slot);
+      }
+    }
+    token_slot[p] = slot;
+  }
+  __syncthreads();
+  // gather: one warp per local pair
+  const int n = npairs;
+  for (int i = warp; i < n; i += kFrontThreads / 32) {
+    const int2 ts = pairs[i];
+    const uint4* src = reinterpret_cast<const uint4*>(hidden + static_cast<size_t>(ts.x) * kH);
+    uint4* dst = reinterpret_cast<uint4*>(a_rows + static_cast<size_t>(ts.y) * kH);
+    uint4 v[kH / 16 / 32];
+#pragma unroll
+    for (int j = 0; j < kH / 16 / 32; ++j) v[j] = src[lane + 32 * j];
+#pragma unroll
+    for (int j = 0; j < kH / 16 / 32; ++j) dst[lane + 32 * j] = v[j];
+    for (int kb = lane; kb < kHB; kb += 32)
+      a_scale[static_cast<size_t>(kb) * p_cap + ts.y] = hidden_scale[static_cast<size_t>(kb) * T + ts.x];
   }
 }
 
@@ -432,11 +579,25 @@ cudaError_t launch_permute_scan(const uint4* chunk_masks, int nchunk, int E, Met
 
 cudaError_t launch_permute_assign(const int32_t* topk_idx, const float* topk_w, const uint4* chunk_masks,
                                   const int32_t* chunk_base, const Meta* meta, int T, int E, int offset, int p_cap,
-                                  int32_t* token_slot, int32_t* slot_token, float* slot_weight, int* status,
-                                  cudaStream_t s) {
+                                  int32_t* token_slot, int32_t* slot_token, float* slot_weight, int32_t* slot_pair,
+                                  int* status, cudaStream_t s) {
   const int nchunk = (T + kChunkTokens - 1) / kChunkTokens;
   permute_assign_kernel<<<nchunk, 256, 0, s>>>(topk_idx, topk_w, chunk_masks, chunk_base, meta, T, E, offset, p_cap,
-                                               token_slot, slot_token, slot_weight, status);
+                                               token_slot, slot_token, slot_weight, slot_pair, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_front_small(const float* logits, const void* bias, float rsf, const int32_t* topk_in,
+                               const float* topk_w_in, const uint8_t* hidden, const float* hidden_scale, int T, int E,
+                               int offset, int p_cap, Meta* meta, int32_t* tile_expert, int32_t* tile_row0,
+                               int32_t* tile_rows, int32_t* ptile_expert, int32_t* ptile_row0, int32_t* ptile_rows,
+                               int32_t* token_slot, int32_t* slot_token, float* slot_weight, int32_t* slot_pair,
+                               uint8_t* a_rows, float* a_scale, int* status, cudaStream_t s) {
+  front_small_kernel<<<1, kFrontThreads, 0, s>>>(logits, static_cast<const __nv_bfloat16*>(bias), rsf, topk_in,
+                                                 topk_w_in, hidden, hidden_scale, T, E, offset, p_cap, meta,
+                                                 tile_expert, tile_row0, tile_rows, ptile_expert, ptile_row0,
+                                                 ptile_rows, token_slot, slot_token, slot_weight, slot_pair, a_rows,
+                                                 a_scale, status);
   return cudaGetLastError();
 }
 
