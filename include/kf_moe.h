@@ -168,7 +168,8 @@ int kf_moe_forward_noalloc(const float* routing_logits, const void* routing_bias
 #define KF_KERNEL_GEMM2 6
 #define KF_KERNEL_REDUCE 7
 #define KF_KERNEL_FRONT_SMALL 8
-#define KF_KERNEL_COUNT 9
+#define KF_KERNEL_SWIGLU_QUANT 9
+#define KF_KERNEL_COUNT 10
 
 /*
  * Profiling.  Between kf_moe_profile_begin() and kf_moe_profile_end(), every
@@ -180,8 +181,9 @@ int kf_moe_forward_noalloc(const float* routing_logits, const void* routing_bias
 int kf_moe_profile_begin(void);
 int kf_moe_profile_end(float* total_ms, int32_t* launches, int32_t n);
 
-/* Diagnostics: number of kernels one kf_moe_forward launches for T > 128 tokens
- * (calls of at most 128 tokens run a single-block front end: 4 kernels). */
+/* Diagnostics: number of kernels one kf_moe_forward launches for T > 64 tokens
+ * (calls of at most 32 tokens run a single-block front end and a split-K GEMM1
+ * finish: 5 kernels; 33..64 tokens: 8). */
 int32_t kf_moe_launches_per_forward(void);
 
 /* Human-readable text for a KF_ERR_* code. */

@@ -227,7 +227,7 @@ def read_status(device: Optional[torch.device] = None) -> int:
 
 
 KERNEL_NAMES = ["route", "masks_from_topk", "permute_scan", "permute_assign", "gather_rows", "gemm1_swiglu",
-                "gemm2_weighted", "unpermute_reduce", "front_small"]
+                "gemm2_weighted", "unpermute_reduce", "front_small", "swiglu_quant"]
 
 
 def profile_begin() -> None:

@@ -47,7 +47,7 @@ constexpr int G1_OFF_B = G1_S * G1_A;
 constexpr int G1_OFF_AS = G1_OFF_B + G1_S * G1_B;
 constexpr int G1_OFF_WS = G1_OFF_AS + kScaleRing * kBlk * 4;
 constexpr int G1_OFF_BAR = G1_OFF_WS + kScaleRing * 8;
-constexpr int G1_NBAR = 2 * G1_S + 2 * kScaleRing + 10;
+constexpr int G1_NBAR = 2 * G1_S + 2 * kScaleRing + 6;
 constexpr int G1_OFF_MISC = G1_OFF_BAR + G1_NBAR * 8;
 constexpr int G1_OFF_XCH = G1_OFF_MISC + 16;
 constexpr int G1_SMEM = G1_OFF_XCH + 2 * 2 * kBlk * 4 + 1024;
@@ -64,7 +64,7 @@ constexpr int G2_OFF_B = 2 * G2_S * G2_A;
 constexpr int G2_OFF_AS = G2_OFF_B + G2_S * G2_B;
 constexpr int G2_OFF_WS = G2_OFF_AS + kScaleRing * kBlk * 4;
 constexpr int G2_OFF_BAR = G2_OFF_WS + kScaleRing * 8;
-constexpr int G2_NBAR = 2 * G2_S + 2 * kScaleRing + 8;
+constexpr int G2_NBAR = 2 * G2_S + 2 * kScaleRing + 4;
 constexpr int G2_OFF_MISC = G2_OFF_BAR + G2_NBAR * 8;
 constexpr int G2_SMEM = G2_OFF_MISC + 16 + 1024;
 constexpr int kG2NB = kH / 256;  // 28 column blocks of 256
@@ -133,37 +133,6 @@ struct ArmedSlots {
   }
 };
 
-// Split-K hand-off among the 8 promotion warps of a CTA after they published
-// their partial sums: the first promotion warp counts this CTA's split in
-// fix_count[key]; returns (to every promotion thread) whether this CTA was the
-// last of the `ksplit` CTAs of that output block -- the one that finishes it.
-// fbar[0] gathers the 8 warps, fbar[1] releases them with the verdict.  Bounded
-// waits; returns -1 if the CTA is aborting.
-__device__ __forceinline__ int split_k_last(uint64_t* fbar, volatile int* fflag, int fx, int pw, int lane,
-                                            int* fix_count, int key, int ksplit, volatile int* abort_flag,
-                                            int* status) {
-  __threadfence();
-  __syncwarp();
-  const uint32_t par = static_cast<uint32_t>(fx >> 1) & 1u;
-  const int slot = fx & 1;
-  if (lane == 0) mbar_arrive(&fbar[2 * slot]);
-  if (pw == 0 && lane == 0) {
-    int verdict = -1;
-    if (mbar_wait_abort(&fbar[2 * slot], par, abort_flag, status, KF_STATUS_TIMEOUT_EPILOGUE)) {
-      const int old = atomicAdd(&fix_count[key], 1);
-      verdict = (old == ksplit - 1) ? 1 : 0;
-      if (verdict) fix_count[key] = 0;  // ready for the next call
-      __threadfence();
-    }
-    fflag[slot] = verdict;
-    mbar_arrive(&fbar[2 * slot + 1]);
-  }
-  if (!mbar_wait_abort(&fbar[2 * slot + 1], par, abort_flag, status, KF_STATUS_TIMEOUT_EPILOGUE)) return -1;
-  const int v = fflag[slot];
-  if (v == 1) __threadfence();
-  return v;
-}
-
 __global__ void __launch_bounds__(kThreads, 1)
     gemm1_swiglu_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_a32,
                         const __grid_constant__ CUtensorMap tm_w, const Gemm1Args g) {
@@ -181,10 +150,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* pfull = sempty + kScaleRing;
   uint64_t* pempty = pfull + 2;
   uint64_t* xbar = pempty + 2;
-  uint64_t* fbar = xbar + 2;  // [2 slots][gather, release]
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + G1_OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + G1_OFF_MISC + 4);
-  volatile int* fflag = reinterpret_cast<volatile int*>(smem + G1_OFF_MISC + 8);
   float* xch = reinterpret_cast<float*>(smem + G1_OFF_XCH);
 
   const int S = g.ksplit;
@@ -206,8 +173,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&pfull[b], 1);
       mbar_init(&pempty[b], kEpiWarps);
       mbar_init(&xbar[b], kEpiWarps);
-      mbar_init(&fbar[2 * b], kEpiWarps);
-      mbar_init(&fbar[2 * b + 1], 1);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -321,7 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = q * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     RingPos ss, pb;
-    int it = 0, fx = 0;  // epilogue and split-K hand-off uses (barrier phases)
+    int it = 0;  // epilogues run so far (phase of the absmax exchange barrier)
     bool ok = true;
     for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
       const int base = u / S, ks = u % S;
@@ -369,9 +334,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       if (S > 1) {
-        // publish this split's fp32 partial sums, then only the last split's CTA goes on
-        const size_t prow = row < nrows ? static_cast<size_t>(g.slot_pair[row0 + row]) : 0;
+        // split-K: store this split's fp32 sums (up | gate) for the pair; the
+        // SwiGLU and requantisation run in swiglu_quant_kernel once all splits are in
         if (row < nrows) {
+          const size_t prow = static_cast<size_t>(g.slot_pair[row0 + row]);
           float4* pu = reinterpret_cast<float4*>(g.partial + (static_cast<size_t>(ks) * g.max_pairs + prow) * 4096 +
                                                  nb * 256 + h * 64);
 #pragma unroll
@@ -380,36 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             pu[32 + j / 2] = make_float4(acc_g[j].x, acc_g[j].y, acc_g[j + 1].x, acc_g[j + 1].y);
           }
         }
-        const int last = split_k_last(fbar, fflag, fx, pw, lane, g.fix_count, base, S, abort_flag, g.status);
-        ++fx;
-        if (last < 0) {
-          ok = false;
-          break;
-        }
-        if (!last) continue;
-        if (row < nrows) {  // sum the splits in split order (deterministic)
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            acc_u[j] = make_float2(0.f, 0.f);
-            acc_g[j] = make_float2(0.f, 0.f);
-          }
-          for (int k2 = 0; k2 < S; ++k2) {
-            const float4* pu = reinterpret_cast<const float4*>(
-                g.partial + (static_cast<size_t>(k2) * g.max_pairs + prow) * 4096 + nb * 256 + h * 64);
-#pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-              const float4 a = pu[j / 2], b = pu[32 + j / 2];
-              acc_u[j].x += a.x;
-              acc_u[j].y += a.y;
-              acc_u[j + 1].x += a.z;
-              acc_u[j + 1].y += a.w;
-              acc_g[j].x += b.x;
-              acc_g[j].y += b.y;
-              acc_g[j + 1].x += b.z;
-              acc_g[j + 1].y += b.w;
-            }
-          }
-        }
+        continue;
       }
       // SwiGLU: silu(X2) * X1 with X1 = up (W13 rows [0, I)), X2 = gate (rows [I, 2I))
       float amax = 0.f;
@@ -479,14 +416,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* sempty = sfull + kScaleRing;
   uint64_t* pfull = sempty + kScaleRing;
   uint64_t* pempty = pfull + 2;
-  uint64_t* fbar = pempty + 2;  // [2 slots][gather, release]
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + G2_OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + G2_OFF_MISC + 4);
-  volatile int* fflag = reinterpret_cast<volatile int*>(smem + G2_OFF_MISC + 8);
 
-  const int S = g.ksplit;
-  const int kb_per = kIB / S;
-  const int num_units = g.meta->num_tiles * kG2NB * S;
+  const int num_units = g.meta->num_tiles * kG2NB;
   if (static_cast<int>(blockIdx.x) >= num_units) return;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -502,8 +435,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&pfull[b], 1);
       mbar_init(&pempty[b], kEpiWarps);
-      mbar_init(&fbar[2 * b], kEpiWarps);
-      mbar_init(&fbar[2 * b + 1], 1);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -528,8 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ArmedSlots armed_st, armed_ss;
       bool ok = true;
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
-        const int base = u / S, ks = u % S;
-        const int tile = base / kG2NB, nb2 = base % kG2NB;
+        const int tile = u / kG2NB, nb2 = u % kG2NB;
         const int e = g.tile_expert[tile];
         const int row0 = g.tile_row0[tile];
         const bool small = g.tile_rows[tile] <= kSmallRows;
@@ -539,7 +469,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float s0 = lane < kIB ? ws[lane] : 0.f;
         const float s1 = lane < kIB ? ws[kIB + lane] : 0.f;
         const int wrow = e * kH + nb2 * 256;
-        for (int kb = ks * kb_per; kb < (ks + 1) * kb_per; ++kb) {
+        for (int kb = 0; kb < kIB; ++kb) {
           const float w0 = __shfl_sync(0xffffffffu, s0, kb);
           const float w1 = __shfl_sync(0xffffffffu, s1, kb);
           int good = 1;
@@ -578,7 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         RingPos st, pb, last;
         bool ok = true, committed = false;
         for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
-          for (int kb = 0; kb < kb_per; ++kb) {
+          for (int kb = 0; kb < kIB; ++kb) {
             if (!mbar_wait_abort(&pempty[pb.idx], pb.ph ^ 1u, abort_flag, g.status, KF_STATUS_TIMEOUT_MMA) ||
                 !mbar_wait_abort(&full[st.idx], st.ph, abort_flag, g.status, KF_STATUS_TIMEOUT_MMA)) {
               ok = false;
@@ -618,18 +548,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = q * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     RingPos ss, pb;
-    int fx = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
-      const int base = u / S, ks = u % S;
-      const int tile = base / kG2NB, nb2 = base % kG2NB;
+      const int tile = u / kG2NB, nb2 = u % kG2NB;
       const int row0 = g.tile_row0[tile];
       const int nrows = g.tile_rows[tile];
       const bool live = q * 32 < nrows;
       float2 acc[64];
 #pragma unroll
       for (int j = 0; j < 64; ++j) acc[j] = make_float2(0.f, 0.f);
-      for (int kb = 0; kb < kb_per; ++kb) {
+      for (int kb = 0; kb < kIB; ++kb) {
         if (!mbar_wait_abort(&sfull[ss.idx], ss.ph, abort_flag, g.status, KF_STATUS_TIMEOUT_EPILOGUE)) {
           ok = false;
           break;
@@ -663,39 +591,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         pb.advance<2>();
       }
       if (!ok) break;
-      if (S > 1) {
-        const size_t prow = row < nrows ? static_cast<size_t>(g.slot_pair[row0 + row]) : 0;
-        if (row < nrows) {
-          float4* pp = reinterpret_cast<float4*>(g.partial + (static_cast<size_t>(ks) * g.max_pairs + prow) * kH +
-                                                 nb2 * 256 + h * 128);
-#pragma unroll
-          for (int j = 0; j < 64; j += 2)
-            pp[j / 2] = make_float4(acc[j].x, acc[j].y, acc[j + 1].x, acc[j + 1].y);
-        }
-        const int last = split_k_last(fbar, fflag, fx, pw, lane, g.fix_count, base, S, abort_flag, g.status);
-        ++fx;
-        if (last < 0) {
-          ok = false;
-          break;
-        }
-        if (!last) continue;
-        if (row < nrows) {
-#pragma unroll
-          for (int j = 0; j < 64; ++j) acc[j] = make_float2(0.f, 0.f);
-          for (int k2 = 0; k2 < S; ++k2) {
-            const float4* pp = reinterpret_cast<const float4*>(
-                g.partial + (static_cast<size_t>(k2) * g.max_pairs + prow) * kH + nb2 * 256 + h * 128);
-#pragma unroll
-            for (int j = 0; j < 64; j += 2) {
-              const float4 a = pp[j / 2];
-              acc[j].x += a.x;
-              acc[j].y += a.y;
-              acc[j + 1].x += a.z;
-              acc[j + 1].y += a.w;
-            }
-          }
-        }
-      }
       if (row < nrows) {
         const float w = g.slot_weight[row0 + row];
         float4* dst = reinterpret_cast<float4*>(g.y + static_cast<size_t>(row0 + row) * kH + nb2 * 256 + h * 128);
@@ -712,6 +607,46 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
+// Split-K finish of GEMM1: sum the splits' fp32 partials of one (row, 128-column
+// block) in split order, apply SwiGLU and the two-term FP8 encoding -- the
+// epilogue of gemm1_swiglu_kernel for calls whose K loop was split.  One warp
+// per (permuted row, column block); lane l owns columns 4l..4l+3 of the block.
+__global__ void __launch_bounds__(256) swiglu_quant_kernel(const Meta* __restrict__ meta,
+                                                           const int32_t* __restrict__ tile_rows,
+                                                           const int32_t* __restrict__ slot_pair,
+                                                           const float* __restrict__ partial, int ksplit,
+                                                           int max_pairs, int p_cap, uint8_t* __restrict__ c_hi,
+                                                           uint8_t* __restrict__ c_lo, float* __restrict__ c_scale) {
+  const int lane = threadIdx.x & 31;
+  const int warps = blockDim.x >> 5;
+  const int nwork = meta->num_tiles * kBlk * kIB;
+  for (int wi = blockIdx.x * warps + (threadIdx.x >> 5); wi < nwork; wi += gridDim.x * warps) {
+    const int r = wi / kIB, nb = wi % kIB;
+    if ((r & (kBlk - 1)) >= tile_rows[r >> 7]) continue;
+    const size_t pair = static_cast<size_t>(slot_pair[r]);
+    float4 up = make_float4(0.f, 0.f, 0.f, 0.f), gt = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < ksplit; ++s) {
+      const float* base = partial + (static_cast<size_t>(s) * max_pairs + pair) * 4096 + nb * 256;
+      // per column block the partial row holds [up 128 | gate 128]
+      const float4 u = reinterpret_cast<const float4*>(base)[lane];
+      const float4 g = reinterpret_cast<const float4*>(base + 128)[lane];
+      up.x += u.x; up.y += u.y; up.z += u.z; up.w += u.w;
+      gt.x += g.x; gt.y += g.y; gt.z += g.z; gt.w += g.w;
+    }
+    float hv[4] = {(gt.x / (1.0f + expf(-gt.x))) * up.x, (gt.y / (1.0f + expf(-gt.y))) * up.y,
+                   (gt.z / (1.0f + expf(-gt.z))) * up.z, (gt.w / (1.0f + expf(-gt.w))) * up.w};
+    float amax = fmaxf(fmaxf(fabsf(hv[0]), fabsf(hv[1])), fmaxf(fabsf(hv[2]), fabsf(hv[3])));
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    const float inv = amax > 0.f ? 448.0f / amax : 1.0f;
+    const uint2 w = encode_hilo4(hv[0] * inv, hv[1] * inv, hv[2] * inv, hv[3] * inv);
+    const size_t off = static_cast<size_t>(r) * kI + nb * kBlk + lane * 4;
+    *reinterpret_cast<uint32_t*>(c_hi + off) = w.x;
+    *reinterpret_cast<uint32_t*>(c_lo + off) = w.y;
+    if (lane == 0) c_scale[static_cast<size_t>(nb) * p_cap + r] = amax > 0.f ? amax / 448.0f : 1.0f;
+  }
+}
+
 }  // namespace
 
 cudaError_t gemm_set_attributes() {
@@ -723,6 +658,12 @@ cudaError_t gemm_set_attributes() {
 cudaError_t launch_gemm1(const CUtensorMap& tm_a, const CUtensorMap& tm_a32, const CUtensorMap& tm_w13,
                          const Gemm1Args& args, int grid, cudaStream_t s) {
   gemm1_swiglu_kernel<<<grid, kThreads, G1_SMEM, s>>>(tm_a, tm_a32, tm_w13, args);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu_quant(const Gemm1Args& g, int grid, cudaStream_t s) {
+  swiglu_quant_kernel<<<grid, 256, 0, s>>>(g.meta, g.tile_rows, g.slot_pair, g.partial, g.ksplit, g.max_pairs,
+                                           g.p_cap, g.c_hi, g.c_lo, g.c_scale);
   return cudaGetLastError();
 }
 

@@ -34,13 +34,12 @@ struct Meta {
 struct Workspace {
   size_t status, meta, topk_idx, topk_w, token_slot, chunk_masks, chunk_base;
   size_t tile_expert, tile_row0, tile_rows, ptile_expert, ptile_row0, ptile_rows, slot_token, slot_weight, slot_pair;
-  size_t a_rows, a_scale, c_hi, c_lo, c_scale, y, partial, fix_count;
+  size_t a_rows, a_scale, c_hi, c_lo, c_scale, y, partial;
   size_t total;
   int32_t p_cap;    // capacity in permuted rows (multiple of 128)
   int32_t nt_cap;   // capacity in row tiles
   int32_t nchunk;   // routing/permute chunks of 128 tokens
-  int32_t ksplit1;  // split-K factors of GEMM1 / GEMM2 (1 = no split)
-  int32_t ksplit2;
+  int32_t ksplit1;  // split-K factor of GEMM1 (1 = no split)
 };
 
 Workspace plan_workspace(int32_t T, int32_t E);
@@ -91,15 +90,13 @@ struct Gemm1Args {
   int32_t p_cap;
   int* status;
   // Split-K (single-CTA kernel only): ksplit CTAs share a (tile, column block),
-  // each over 56/ksplit K chunks; their fp32 partial sums go to `partial`
-  // ([ksplit][max_pairs][4096], indexed by the pair id slot_pair[row]) and the
-  // last CTA to finish (counted in fix_count) sums them in split order and runs
-  // the epilogue.
+  // each over 56/ksplit K chunks, and store their fp32 partial sums in `partial`
+  // ([ksplit][max_pairs][4096], indexed by the pair id slot_pair[row]);
+  // swiglu_quant_kernel then sums them in split order and runs the epilogue.
   int32_t ksplit;
   int32_t max_pairs;
   const int32_t* slot_pair;
   float* partial;
-  int* fix_count;
 };
 
 struct Gemm2Args {
@@ -113,11 +110,6 @@ struct Gemm2Args {
   float* y;                 // [p_cap][7168]
   int32_t p_cap;
   int* status;
-  int32_t ksplit;           // as in Gemm1Args; partial is [ksplit][max_pairs][7168]
-  int32_t max_pairs;
-  const int32_t* slot_pair;
-  float* partial;
-  int* fix_count;
 };
 
 cudaError_t launch_gemm1(const CUtensorMap& tm_a, const CUtensorMap& tm_a32, const CUtensorMap& tm_w13,
@@ -130,6 +122,8 @@ cudaError_t launch_gemm1_pair(const CUtensorMap& tm_a, const CUtensorMap& tm_a32
 cudaError_t launch_gemm2_pair(const CUtensorMap& tm_chi, const CUtensorMap& tm_clo, const CUtensorMap& tm_chi32,
                               const CUtensorMap& tm_clo32, const CUtensorMap& tm_w2, const Gemm2Args& args, int grid,
                               cudaStream_t s);
+// Split-K finish of GEMM1 (sum of the splits, SwiGLU, hi/lo encoding).
+cudaError_t launch_swiglu_quant(const Gemm1Args& g, int grid, cudaStream_t s);
 cudaError_t gemm_set_attributes();
 cudaError_t gemm_pair_set_attributes();
 // Co-resident 2-CTA clusters of the pair kernels on the current device (0 if unknown).

@@ -7,7 +7,6 @@
 
 #include <cstdio>
 #include <cstdlib>
-#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -167,8 +166,9 @@ int check_common(int32_t T, int32_t E, int32_t offset) {
   return KF_OK;
 }
 
-// Calls of at most this many tokens run the single-block front end.
-constexpr int kSmallT = kChunkTokens;
+// Calls of at most this many tokens run the single-block front end (it gathers
+// rows on one SM, which stops paying off beyond a few dozen tokens).
+constexpr int kSmallT = 32;
 
 // Permutation (unless the single-block front end already did it), both grouped
 // GEMMs and the reduce, from chunk masks already in the workspace.
@@ -243,10 +243,6 @@ int run_experts(const Workspace& w, void* ws, const int32_t* topk_idx, const flo
   g1.max_pairs = T * kTopK;
   g1.slot_pair = ws_ptr<int32_t>(ws, w.slot_pair);
   g1.partial = ws_ptr<float>(ws, w.partial);
-  g1.fix_count = ws_ptr<int>(ws, w.fix_count);
-  if ((g1.ksplit > 1 || (!pair && w.ksplit2 > 1)) &&
-      cudaMemsetAsync(g1.fix_count, 0, static_cast<size_t>(w.nt_cap) * (kH / 256) * 4, s) != cudaSuccess)
-    return KF_ERR_CUDA;
   {
     ProfScope ps(KF_KERNEL_GEMM1, s);
     cudaError_t e;
@@ -260,6 +256,10 @@ int run_experts(const Workspace& w, void* ws, const int32_t* topk_idx, const flo
     }
     if (e != cudaSuccess) return KF_ERR_CUDA;
   }
+  if (g1.ksplit > 1) {
+    ProfScope ps(KF_KERNEL_SWIGLU_QUANT, s);
+    if (launch_swiglu_quant(g1, num_sms, s) != cudaSuccess) return KF_ERR_CUDA;
+  }
 
   Gemm2Args g2;
   g2.meta = meta;
@@ -272,11 +272,7 @@ int run_experts(const Workspace& w, void* ws, const int32_t* topk_idx, const flo
   g2.y = ws_ptr<float>(ws, w.y);
   g2.p_cap = w.p_cap;
   g2.status = status;
-  g2.ksplit = pair ? 1 : w.ksplit2;
-  g2.max_pairs = T * kTopK;
-  g2.slot_pair = g1.slot_pair;
-  g2.partial = g1.partial;
-  g2.fix_count = g1.fix_count;
+
   {
     ProfScope ps(KF_KERNEL_GEMM2, s);
     cudaError_t e;
@@ -285,8 +281,7 @@ int run_experts(const Workspace& w, void* ws, const int32_t* topk_idx, const flo
       const int clusters = units < pair_clusters ? units : pair_clusters;
       e = launch_gemm2_pair(tm_chi, tm_clo, tm_chi32, tm_clo32, tm_w2_half, g2, 2 * clusters, s);
     } else {
-      const int units_k = units * g2.ksplit;
-      e = launch_gemm2(tm_chi, tm_clo, tm_chi32, tm_clo32, tm_w2, g2, units_k < num_sms ? units_k : num_sms, s);
+      e = launch_gemm2(tm_chi, tm_clo, tm_chi32, tm_clo32, tm_w2, g2, units < num_sms ? units : num_sms, s);
     }
     if (e != cudaSuccess) return KF_ERR_CUDA;
   }
@@ -357,14 +352,12 @@ Workspace plan_workspace(int32_t T, int32_t E) {
   w.c_lo = take(pc * kI);
   w.c_scale = take(pc * kIB * 4);
   w.y = take(pc * kH * 4);
-  // split-K for decode-sized calls: fewer tiles than SMs otherwise leave most SMs
-  // idle and quantise the weight stream into ~2 waves
+  // split-K of GEMM1 for decode-sized calls: with one row tile per active expert
+  // its 16 column blocks per tile give about one wave of units, which a 4-way K
+  // split turns into four shorter, evenly filled waves
   w.ksplit1 = T <= kSplitKMaxT ? 4 : 1;
-  w.ksplit2 = T <= kSplitKMaxT ? 2 : 1;
   const size_t max_pairs = static_cast<size_t>(T) * kTopK;
-  const size_t split_cols = std::max(static_cast<size_t>(w.ksplit1) * kI * 2, static_cast<size_t>(w.ksplit2) * kH);
-  w.partial = take(w.ksplit1 > 1 || w.ksplit2 > 1 ? split_cols * max_pairs * 4 : 0);
-  w.fix_count = take(static_cast<size_t>(w.nt_cap) * (kH / 256) * 4);
+  w.partial = take(w.ksplit1 > 1 ? static_cast<size_t>(w.ksplit1) * 2 * kI * max_pairs * 4 : 0);
   w.total = off;
   return w;
 }
