@@ -52,6 +52,7 @@ def parse():
     p.add_argument("--workload", default="ep", choices=["ep", "prefill", "decode"])
     p.add_argument("--tokens", type=int, default=None)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--graph", action="store_true", help="replay the layer as a CUDA graph (1 GPU)")
     return p.parse_args()
 
 
@@ -227,6 +228,11 @@ def main():
         def step(logits, bias, hid, hs):
             return B.kernel(logits, bias, hid, hs, wb.gemm1_weights, wb.gemm1_weights_scale, wb.gemm2_weights,
                             wb.gemm2_weights_scale, offset, 2.5)
+    profiled_step = step
+    if args.graph and world == 1:
+        from kernelforge_b200.graph import GraphedMoE
+        graphed = GraphedMoE(wb, offset, 2.5, T).capture()
+        step = graphed
 
     # local (token, expert) pairs of this rank's GEMMs (for the FLOP count)
     idx, _ = B.route(ti.routing_logits, ti.routing_bias, 2.5)
@@ -253,9 +259,10 @@ def main():
         if profile:
             B.profile_begin()
         ev0.record(stream)
+        fn = profiled_step if profile else step
         for k in range(k_steps):
             sev[k][0].record(stream)
-            step(ti.routing_logits, ti.routing_bias, ti.hidden_states, ti.hidden_states_scale)
+            fn(ti.routing_logits, ti.routing_bias, ti.hidden_states, ti.hidden_states_scale)
             sev[k][1].record(stream)
         ev1.record(stream)
         torch.cuda.synchronize(dev)
@@ -274,6 +281,7 @@ def main():
         t = torch.tensor([ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = float(t.item())
+        pairs = layer.local_pairs()   # rank 0's GEMM rows in the last step
     ms_per_step = ms / args.steps
     value = world * T * args.steps / (ms / 1e3)
 
@@ -343,7 +351,7 @@ def main():
             "config": {"workload": name, "tokens_per_gpu": T, "local_experts_per_gpu": E,
                        "global_experts": E_GLOBAL, "hidden": H, "intermediate": I, "top_k": 8,
                        "parallelism": f"ep{world}", "l2": "inputs larger than L2 (weights stream from HBM)",
-                       "pairs_rank0": pairs},
+                       "pairs_rank0": pairs, "cuda_graph": bool(args.graph and world == 1)},
             "p50_step_ms": step_ms[len(step_ms) // 2], "p90_step_ms": step_ms[int(len(step_ms) * 0.9)],
             "tflops_per_gpu": (FLOP_PER_PAIR * pairs / (ms_per_step / 1e3) / 1e12) if pairs else None,
             "roofline": roofline, "kernels": kernels, "gpu_launches": total_launches,

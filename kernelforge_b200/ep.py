@@ -127,6 +127,14 @@ class ExpertParallelMoE:
         self.experts_fn = experts_fn
         self.route_fn = route_fn
 
+    def local_pairs(self) -> int:
+        """(row, local expert) pairs this rank's expert kernels processed in the last forward (synchronises)."""
+        ids = getattr(self, "_last_ids", None)
+        if ids is None:
+            return 0
+        loc = ids.to(torch.int64) - self.offset
+        return int(((ids >= 0) & (loc >= 0) & (loc < self.num_local)).sum().item())
+
     def forward(self, routing_logits, routing_bias, hidden_states, hidden_states_scale, routed_scaling_factor):
         T = routing_logits.shape[0]
         idx, w = self.route_fn(routing_logits, routing_bias, routed_scaling_factor)
@@ -138,6 +146,7 @@ class ExpertParallelMoE:
         recv = torch.empty((sum(r_split), ROW_BYTES), dtype=torch.uint8, device=send.device)
         dist.all_to_all_single(recv, send, output_split_sizes=r_split, input_split_sizes=s_split, group=self.group)
         hid, sc, ids, ww = unpack_rows(recv)
+        self._last_ids = ids
         part = self.experts_fn(ids, ww, hid, sc, self.w.gemm1_weights, self.w.gemm1_weights_scale,
                                self.w.gemm2_weights, self.w.gemm2_weights_scale, self.offset,
                                out_dtype=self.combine_dtype)
