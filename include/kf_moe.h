@@ -113,6 +113,47 @@ int kf_moe_experts(const int32_t* topk_idx, const float* topk_weight,
                    void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Experts on rows in the expert-parallel packed layout: `rows` holds num_rows
+ * rows of 7456 bytes (FP8 hidden row [7168] | f32 scales [56] | int32 global
+ * expert ids [8], -1 = none | f32 weights [8]), as kf_ep_dispatch writes them
+ * and the all-to-all delivers them.  Same computation as kf_moe_experts, read
+ * in place (no unpacking copy).  Expert-parallel receive side; the reference
+ * has no multi-GPU path (its data contract's local_expert_offset,
+ * kernel.py:1826, is what the shards use).
+ */
+int kf_moe_experts_packed(const void* rows, const void* gemm1_weights, const float* gemm1_weights_scale,
+                          const void* gemm2_weights, const float* gemm2_weights_scale, int32_t num_rows,
+                          int32_t num_local_experts, int32_t local_expert_offset, void* output, int32_t output_fp32,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Expert-parallel dispatch (no reference counterpart: the reference has no
+ * multi-GPU code).  Rank r of `world` owns experts [r*256/world, (r+1)*256/world).
+ * For the rank's T routed tokens (topk_idx/topk_weight [T, 8], hidden [T, 7168],
+ * scales [56, T]) writes:
+ *   send_rows   [kf_ep_max_send_rows(T, world)][7456]: one packed row per (token,
+ *               destination owning >= 1 of its experts), grouped by destination,
+ *               token order inside a destination; ids the destination does not
+ *               own are -1 (weight 0)
+ *   send_counts int64 [world] (device): rows per destination
+ *   pos         int32 [T, world]: row of (token, destination), -1 if not sent
+ * `workspace`: kf_ep_workspace_bytes(T, world) bytes.  world divides 256, <= 64.
+ */
+size_t kf_ep_workspace_bytes(int32_t num_tokens, int32_t world);
+int32_t kf_ep_max_send_rows(int32_t num_tokens, int32_t world);
+int kf_ep_dispatch(const int32_t* topk_idx, const float* topk_weight, const void* hidden_states,
+                   const float* hidden_states_scale, int32_t num_tokens, int32_t world, void* send_rows,
+                   int64_t* send_counts, int32_t* pos, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Expert-parallel combine: output[t] (bf16 [T, 7168]) = sum over destinations d
+ * in ascending order of partials[pos[t, d]] (rows of bf16, or f32 when
+ * partials_fp32), accumulated in f32 and rounded once.
+ */
+int kf_ep_combine(const void* partials, int32_t partials_fp32, const int32_t* pos, int32_t num_tokens,
+                  int32_t world, void* output, void* stream);
+
+/*
  * Synchronises `stream`, then copies the device status word of the last call
  * that used `workspace` into *status (host pointer) and clears it.  Returns
  * KF_ERR_DEVICE_STATUS if any bit was set.

@@ -58,6 +58,16 @@ def _load():
         lib.kf_moe_error_string.argtypes = [ctypes.c_int]
         lib.kf_moe_launches_per_forward.restype = i32
         lib.kf_moe_launches_per_forward.argtypes = []
+        lib.kf_moe_experts_packed.restype = ctypes.c_int
+        lib.kf_moe_experts_packed.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32, vp, i32, vp, sz, vp]
+        lib.kf_ep_workspace_bytes.restype = sz
+        lib.kf_ep_workspace_bytes.argtypes = [i32, i32]
+        lib.kf_ep_max_send_rows.restype = i32
+        lib.kf_ep_max_send_rows.argtypes = [i32, i32]
+        lib.kf_ep_dispatch.restype = ctypes.c_int
+        lib.kf_ep_dispatch.argtypes = [vp, vp, vp, vp, i32, i32, vp, vp, vp, vp, sz, vp]
+        lib.kf_ep_combine.restype = ctypes.c_int
+        lib.kf_ep_combine.argtypes = [vp, i32, vp, i32, i32, vp, vp]
         lib.kf_moe_profile_begin.restype = ctypes.c_int
         lib.kf_moe_profile_begin.argtypes = []
         lib.kf_moe_profile_end.restype = ctypes.c_int
@@ -242,3 +252,75 @@ def profile_end() -> dict:
     cnt = (ctypes.c_int32 * n)()
     _check(_load().kf_moe_profile_end(ms, cnt, n), "kf_moe_profile_end")
     return {KERNEL_NAMES[i]: (float(ms[i]), int(cnt[i])) for i in range(n)}
+
+
+PACKED_ROW_BYTES = H + (H // 128) * 4 + TOP_K * 4 + TOP_K * 4   # 7456
+
+
+def experts_packed(rows, gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
+                   local_expert_offset, out_dtype=torch.bfloat16):
+    """Experts on packed expert-parallel rows (uint8 ``[R, 7456]``, as ``ep_dispatch`` writes them)."""
+    device = rows.device
+    R = int(rows.shape[0])
+    if rows.dtype != torch.uint8 or rows.dim() != 2 or rows.shape[1] != PACKED_ROW_BYTES:
+        raise ValueError("rows must be uint8 [R, 7456]")
+    rows = rows.contiguous()
+    E, w13, w13s, w2, w2s = _weights(gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, device)
+    out = torch.empty((R, H), dtype=out_dtype, device=device)
+    if R == 0:
+        return out
+    stream = torch.cuda.current_stream(device)
+    ws = workspace(R, E, device, stream)
+    rc = _load().kf_moe_experts_packed(_ptr(rows), _ptr(w13), _ptr(w13s), _ptr(w2), _ptr(w2s), R, E,
+                                       _scalar_int(local_expert_offset), _ptr(out),
+                                       1 if out_dtype == torch.float32 else 0, _ptr(ws), ctypes.c_size_t(ws.numel()),
+                                       ctypes.c_void_p(stream.cuda_stream))
+    _check(rc, "kf_moe_experts_packed")
+    return out
+
+
+_ep_ws: dict = {}
+
+
+def ep_dispatch(topk_idx, topk_weight, hidden_states, hidden_states_scale, world: int):
+    """Device-side expert-parallel dispatch: ``(send_rows [S_max, 7456] u8, send_counts i64 [world], pos i32 [T, world])``."""
+    device = hidden_states.device
+    T = int(hidden_states.shape[0])
+    lib = _load()
+    idx = _expect(topk_idx, "topk_idx", torch.int32, (T, TOP_K), device)
+    w = _expect(topk_weight, "topk_weight", torch.float32, (T, TOP_K), device)
+    hid = _expect(hidden_states, "hidden_states", torch.float8_e4m3fn, (T, H), device)
+    hs = _expect(hidden_states_scale, "hidden_states_scale", torch.float32, (H // 128, T), device)
+    send = torch.empty((int(lib.kf_ep_max_send_rows(T, world)), PACKED_ROW_BYTES), dtype=torch.uint8, device=device)
+    counts = torch.empty((world,), dtype=torch.int64, device=device)
+    pos = torch.empty((T, world), dtype=torch.int32, device=device)
+    stream = torch.cuda.current_stream(device)
+    need = int(lib.kf_ep_workspace_bytes(T, world))
+    key = (device.index, stream.cuda_stream)
+    buf = _ep_ws.get(key)
+    if buf is None or buf.numel() < need:
+        buf = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
+        _ep_ws[key] = buf
+    rc = lib.kf_ep_dispatch(_ptr(idx), _ptr(w), _ptr(hid), _ptr(hs), T, int(world), _ptr(send), _ptr(counts),
+                            _ptr(pos), _ptr(buf), ctypes.c_size_t(buf.numel()), ctypes.c_void_p(stream.cuda_stream))
+    _check(rc, "kf_ep_dispatch")
+    return send, counts, pos
+
+
+def ep_combine(partials, pos, world: int):
+    """bf16 ``[T, 7168]``: per token, the sum of its destinations' partial rows in ascending rank order."""
+    device = pos.device
+    T = int(pos.shape[0])
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=device)
+    if T == 0:
+        return out
+    if partials.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError("partials must be bf16 or f32")
+    partials = partials.contiguous()
+    pos = pos.to(torch.int32).contiguous()
+    stream = torch.cuda.current_stream(device)
+    rc = _load().kf_ep_combine(_ptr(partials) if partials.numel() else ctypes.c_void_p(0),
+                               1 if partials.dtype == torch.float32 else 0, _ptr(pos), T, int(world), _ptr(out),
+                               ctypes.c_void_p(stream.cuda_stream))
+    _check(rc, "kf_ep_combine")
+    return out

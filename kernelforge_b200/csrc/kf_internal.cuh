@@ -49,29 +49,61 @@ inline T* ws_ptr(void* base, size_t off) {
   return reinterpret_cast<T*>(static_cast<char*>(base) + off);
 }
 
+// Where the per-token inputs of the expert stage live.  The reference layout is
+// topk [T][8], hidden [T][7168] and K-major scales [56][T]; the expert-parallel
+// receive buffer holds one 7456-byte row per token (hidden | 56 scales | 8 ids |
+// 8 weights).  Element (t, k) of a field is base[t * token_stride + k * inner_stride].
+struct RowLayout {
+  const int32_t* topk_idx;
+  const float* topk_w;
+  int64_t topk_stride;          // elements between consecutive tokens' 8 ids / weights
+  const uint8_t* hidden;
+  int64_t hidden_stride;        // bytes between consecutive tokens' rows
+  const float* scale;
+  int64_t scale_token_stride;   // elements
+  int64_t scale_kb_stride;      // elements
+  __device__ __forceinline__ int32_t idx(int t, int k) const { return topk_idx[t * topk_stride + k]; }
+  __device__ __forceinline__ float w(int t, int k) const { return topk_w[t * topk_stride + k]; }
+  __device__ __forceinline__ const uint8_t* row(int t) const { return hidden + t * hidden_stride; }
+  __device__ __forceinline__ float sc(int t, int kb) const { return scale[t * scale_token_stride + kb * scale_kb_stride]; }
+};
+
+constexpr int64_t kPackedRowBytes = kH + kHB * 4 + kTopK * 4 + kTopK * 4;  // 7456
+
+inline RowLayout reference_layout(const int32_t* topk_idx, const float* topk_w, const void* hidden,
+                                  const float* hidden_scale, int T) {
+  return RowLayout{topk_idx, topk_w, kTopK, static_cast<const uint8_t*>(hidden), kH, hidden_scale, 1, T};
+}
+
+inline RowLayout packed_layout(const void* rows) {
+  const uint8_t* b = static_cast<const uint8_t*>(rows);
+  return RowLayout{reinterpret_cast<const int32_t*>(b + kH + kHB * 4),
+                   reinterpret_cast<const float*>(b + kH + kHB * 4 + kTopK * 4), kPackedRowBytes / 4, b,
+                   kPackedRowBytes, reinterpret_cast<const float*>(b + kH), kPackedRowBytes / 4, 1};
+}
+
 // Kernel launchers (return cudaGetLastError()).
 cudaError_t launch_route(const float* logits, const void* bias, int T, float rsf, int32_t* topk_idx,
                          float* topk_w, int E, int offset, uint4* chunk_masks, cudaStream_t s);
-cudaError_t launch_masks_from_topk(const int32_t* topk_idx, int T, int E, int offset, uint4* chunk_masks,
-                                   int* status, cudaStream_t s);
+cudaError_t launch_masks_from_topk(const RowLayout& in, int T, int E, int offset, uint4* chunk_masks, int* status,
+                                   cudaStream_t s);
 cudaError_t launch_permute_scan(const uint4* chunk_masks, int nchunk, int E, Meta* meta, int32_t* chunk_base,
                                 int32_t* tile_expert, int32_t* tile_row0, int32_t* tile_rows, int32_t* ptile_expert,
                                 int32_t* ptile_row0, int32_t* ptile_rows, int nt_cap, int* status, cudaStream_t s);
-cudaError_t launch_permute_assign(const int32_t* topk_idx, const float* topk_w, const uint4* chunk_masks,
-                                  const int32_t* chunk_base, const Meta* meta, int T, int E, int offset, int p_cap,
-                                  int32_t* token_slot, int32_t* slot_token, float* slot_weight, int32_t* slot_pair,
-                                  int* status, cudaStream_t s);
+cudaError_t launch_permute_assign(const RowLayout& in, const uint4* chunk_masks, const int32_t* chunk_base,
+                                  const Meta* meta, int T, int E, int offset, int p_cap, int32_t* token_slot,
+                                  int32_t* slot_token, float* slot_weight, int32_t* slot_pair, int* status,
+                                  cudaStream_t s);
 // Single-block front end for T <= kChunkTokens: routing (logits != nullptr) or the
 // caller's routing (topk_in), tile lists, slots and the row gather.
-cudaError_t launch_front_small(const float* logits, const void* bias, float rsf, const int32_t* topk_in,
-                               const float* topk_w_in, const uint8_t* hidden, const float* hidden_scale, int T, int E,
+cudaError_t launch_front_small(const float* logits, const void* bias, float rsf, const RowLayout& in, int T, int E,
                                int offset, int p_cap, Meta* meta, int32_t* tile_expert, int32_t* tile_row0,
                                int32_t* tile_rows, int32_t* ptile_expert, int32_t* ptile_row0, int32_t* ptile_rows,
                                int32_t* token_slot, int32_t* slot_token, float* slot_weight, int32_t* slot_pair,
                                uint8_t* a_rows, float* a_scale, int* status, cudaStream_t s);
 cudaError_t launch_gather_rows(const Meta* meta, const int32_t* tile_rows, const int32_t* slot_token,
-                               const uint8_t* hidden, const float* hidden_scale, int T, int p_cap, uint8_t* a_rows,
-                               float* a_scale, int grid, cudaStream_t s);
+                               const RowLayout& in, int p_cap, uint8_t* a_rows, float* a_scale, int grid,
+                               cudaStream_t s);
 cudaError_t launch_reduce(const int32_t* token_slot, const float* y, int T, void* out, int out_fp32,
                           cudaStream_t s);
 

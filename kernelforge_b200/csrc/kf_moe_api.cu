@@ -172,9 +172,8 @@ constexpr int kSmallT = 32;
 
 // Permutation (unless the single-block front end already did it), both grouped
 // GEMMs and the reduce, from chunk masks already in the workspace.
-int run_experts(const Workspace& w, void* ws, const int32_t* topk_idx, const float* topk_w, const void* hidden,
-                const float* hidden_scale, const void* w13, const float* w13_scale, const void* w2,
-                const float* w2_scale, int T, int E, int offset, void* out, int out_fp32, int num_sms,
+int run_experts(const Workspace& w, void* ws, const RowLayout& in, const void* w13, const float* w13_scale,
+                const void* w2, const float* w2_scale, int T, int E, int offset, void* out, int out_fp32, int num_sms,
                 int pair_clusters, bool front_done, cudaStream_t s) {
   int* status = ws_ptr<int>(ws, w.status);
   Meta* meta = ws_ptr<Meta>(ws, w.meta);
@@ -189,7 +188,7 @@ int run_experts(const Workspace& w, void* ws, const int32_t* topk_idx, const flo
   }
   if (!front_done) {
     ProfScope ps(KF_KERNEL_PERMUTE_ASSIGN, s);
-    if (launch_permute_assign(topk_idx, topk_w, ws_ptr<uint4>(ws, w.chunk_masks), ws_ptr<int32_t>(ws, w.chunk_base),
+    if (launch_permute_assign(in, ws_ptr<uint4>(ws, w.chunk_masks), ws_ptr<int32_t>(ws, w.chunk_base),
                               meta, T, E, offset, w.p_cap, ws_ptr<int32_t>(ws, w.token_slot),
                               ws_ptr<int32_t>(ws, w.slot_token), ws_ptr<float>(ws, w.slot_weight),
                               ws_ptr<int32_t>(ws, w.slot_pair), status, s) != cudaSuccess)
@@ -197,8 +196,7 @@ int run_experts(const Workspace& w, void* ws, const int32_t* topk_idx, const flo
   }
   if (!front_done) {
     ProfScope ps(KF_KERNEL_GATHER_ROWS, s);
-    if (launch_gather_rows(meta, ws_ptr<int32_t>(ws, w.tile_rows), ws_ptr<int32_t>(ws, w.slot_token),
-                           static_cast<const uint8_t*>(hidden), hidden_scale, T, w.p_cap,
+    if (launch_gather_rows(meta, ws_ptr<int32_t>(ws, w.tile_rows), ws_ptr<int32_t>(ws, w.slot_token), in, w.p_cap,
                            ws_ptr<uint8_t>(ws, w.a_rows), ws_ptr<float>(ws, w.a_scale), 4 * num_sms,
                            s) != cudaSuccess)
       return KF_ERR_CUDA;
@@ -296,11 +294,10 @@ int run_experts(const Workspace& w, void* ws, const int32_t* topk_idx, const flo
 }
 
 int run_front_small(const Workspace& w, void* ws, const float* logits, const void* bias, float rsf,
-                    const int32_t* topk_in, const float* topk_w_in, const void* hidden, const float* hidden_scale,
-                    int T, int E, int offset, cudaStream_t s) {
+                    const RowLayout& in, int T, int E, int offset, cudaStream_t s) {
   ProfScope ps(KF_KERNEL_FRONT_SMALL, s);
-  return launch_front_small(logits, bias, rsf, topk_in, topk_w_in, static_cast<const uint8_t*>(hidden), hidden_scale,
-                            T, E, offset, w.p_cap, ws_ptr<Meta>(ws, w.meta), ws_ptr<int32_t>(ws, w.tile_expert),
+  return launch_front_small(logits, bias, rsf, in, T, E, offset, w.p_cap, ws_ptr<Meta>(ws, w.meta),
+                            ws_ptr<int32_t>(ws, w.tile_expert),
                             ws_ptr<int32_t>(ws, w.tile_row0), ws_ptr<int32_t>(ws, w.tile_rows),
                             ws_ptr<int32_t>(ws, w.ptile_expert), ws_ptr<int32_t>(ws, w.ptile_row0),
                             ws_ptr<int32_t>(ws, w.ptile_rows), ws_ptr<int32_t>(ws, w.token_slot),
@@ -430,9 +427,10 @@ int kf_moe_forward(const float* routing_logits, const void* routing_bias, const 
   int32_t* topk_idx = ws_ptr<int32_t>(workspace, w.topk_idx);
   float* topk_w = ws_ptr<float>(workspace, w.topk_w);
   const bool small = T <= kSmallT;
+  const RowLayout in = reference_layout(topk_idx, topk_w, hidden_states, hidden_states_scale, T);
   if (small) {
-    rc = run_front_small(w, workspace, routing_logits, routing_bias, routed_scaling_factor, nullptr, nullptr,
-                         hidden_states, hidden_states_scale, T, E, local_expert_offset, s);
+    rc = run_front_small(w, workspace, routing_logits, routing_bias, routed_scaling_factor, in, T, E,
+                         local_expert_offset, s);
     if (rc != KF_OK) return rc;
   } else {
     ProfScope ps(KF_KERNEL_ROUTE, s);
@@ -440,24 +438,26 @@ int kf_moe_forward(const float* routing_logits, const void* routing_bias, const 
                      local_expert_offset, ws_ptr<uint4>(workspace, w.chunk_masks), s) != cudaSuccess)
       return KF_ERR_CUDA;
   }
-  return run_experts(w, workspace, topk_idx, topk_w, hidden_states, hidden_states_scale, gemm1_weights,
-                     gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, T, E, local_expert_offset, output, 0,
-                     sms, pair_clusters, small, s);
+  return run_experts(w, workspace, in, gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, T, E,
+                     local_expert_offset, output, 0, sms, pair_clusters, small, s);
 }
 
-int kf_moe_experts(const int32_t* topk_idx, const float* topk_weight, const void* hidden_states,
-                   const float* hidden_states_scale, const void* gemm1_weights, const float* gemm1_weights_scale,
-                   const void* gemm2_weights, const float* gemm2_weights_scale, int32_t num_tokens,
-                   int32_t num_local_experts, int32_t local_expert_offset, void* output, int32_t output_fp32,
-                   void* workspace, size_t workspace_bytes, void* stream) {
-  const int T = num_tokens, E = num_local_experts;
-  int rc = check_common(T, E, local_expert_offset);
+}  // extern "C"
+
+namespace kf {
+namespace {
+
+// Experts on rows in `in` (reference or packed layout): the shared body of
+// kf_moe_experts and kf_moe_experts_packed.
+int experts_common(const RowLayout& in, const void* gemm1_weights, const float* gemm1_weights_scale,
+                   const void* gemm2_weights, const float* gemm2_weights_scale, int32_t T, int32_t E, int32_t offset,
+                   void* output, int32_t output_fp32, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_common(T, E, offset);
   if (rc != KF_OK) return rc;
   if (T == 0) return KF_OK;
-  if (!topk_idx || !topk_weight || !hidden_states || !hidden_states_scale || !gemm1_weights ||
-      !gemm1_weights_scale || !gemm2_weights || !gemm2_weights_scale || !output || !workspace)
+  if (!gemm1_weights || !gemm1_weights_scale || !gemm2_weights || !gemm2_weights_scale || !output || !workspace)
     return KF_ERR_INVALID_ARGUMENT;
-  if (!aligned16(hidden_states) || !aligned16(gemm1_weights) || !aligned16(gemm2_weights) || !aligned16(output) ||
+  if (!aligned16(in.hidden) || !aligned16(gemm1_weights) || !aligned16(gemm2_weights) || !aligned16(output) ||
       !aligned16(workspace))
     return KF_ERR_INVALID_ARGUMENT;
   const Workspace w = plan_workspace(T, E);
@@ -470,18 +470,43 @@ int kf_moe_experts(const int32_t* topk_idx, const float* topk_weight, const void
   if (cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess) return KF_ERR_CUDA;
   const bool small = T <= kSmallT;
   if (small) {
-    rc = run_front_small(w, workspace, nullptr, nullptr, 0.f, topk_idx, topk_weight, hidden_states,
-                         hidden_states_scale, T, E, local_expert_offset, s);
+    rc = run_front_small(w, workspace, nullptr, nullptr, 0.f, in, T, E, offset, s);
     if (rc != KF_OK) return rc;
   } else {
     ProfScope ps(KF_KERNEL_MASKS, s);
-    if (launch_masks_from_topk(topk_idx, T, E, local_expert_offset, ws_ptr<uint4>(workspace, w.chunk_masks),
-                               status, s) != cudaSuccess)
+    if (launch_masks_from_topk(in, T, E, offset, ws_ptr<uint4>(workspace, w.chunk_masks), status, s) != cudaSuccess)
       return KF_ERR_CUDA;
   }
-  return run_experts(w, workspace, topk_idx, topk_weight, hidden_states, hidden_states_scale, gemm1_weights,
-                     gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, T, E, local_expert_offset, output,
-                     output_fp32 ? 1 : 0, sms, pair_clusters, small, s);
+  return run_experts(w, workspace, in, gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, T, E,
+                     offset, output, output_fp32 ? 1 : 0, sms, pair_clusters, small, s);
+}
+
+}  // namespace
+}  // namespace kf
+
+extern "C" {
+
+int kf_moe_experts(const int32_t* topk_idx, const float* topk_weight, const void* hidden_states,
+                   const float* hidden_states_scale, const void* gemm1_weights, const float* gemm1_weights_scale,
+                   const void* gemm2_weights, const float* gemm2_weights_scale, int32_t num_tokens,
+                   int32_t num_local_experts, int32_t local_expert_offset, void* output, int32_t output_fp32,
+                   void* workspace, size_t workspace_bytes, void* stream) {
+  if (num_tokens > 0 && (!topk_idx || !topk_weight || !hidden_states || !hidden_states_scale))
+    return KF_ERR_INVALID_ARGUMENT;
+  return experts_common(reference_layout(topk_idx, topk_weight, hidden_states, hidden_states_scale, num_tokens),
+                        gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, num_tokens,
+                        num_local_experts, local_expert_offset, output, output_fp32, workspace, workspace_bytes,
+                        stream);
+}
+
+int kf_moe_experts_packed(const void* rows, const void* gemm1_weights, const float* gemm1_weights_scale,
+                          const void* gemm2_weights, const float* gemm2_weights_scale, int32_t num_rows,
+                          int32_t num_local_experts, int32_t local_expert_offset, void* output, int32_t output_fp32,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  if (num_rows > 0 && !rows) return KF_ERR_INVALID_ARGUMENT;
+  return experts_common(packed_layout(rows), gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
+                        num_rows, num_local_experts, local_expert_offset, output, output_fp32, workspace,
+                        workspace_bytes, stream);
 }
 
 int kf_moe_profile_begin(void) {

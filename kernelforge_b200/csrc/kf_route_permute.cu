@@ -172,9 +172,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const float* __res
 }
 
 // Token bitmasks per local expert from externally supplied routing (expert-parallel receive side).
-__global__ void __launch_bounds__(256) masks_from_topk_kernel(const int32_t* __restrict__ topk_idx, int T, int E,
-                                                              int offset, uint4* __restrict__ chunk_masks,
-                                                              int* status) {
+__global__ void __launch_bounds__(256) masks_from_topk_kernel(const RowLayout in, int T, int E, int offset,
+                                                              uint4* __restrict__ chunk_masks, int* status) {
   __shared__ uint32_t masks[kMaxLocalExperts * 4];
   const int chunk = blockIdx.x;
   for (int i = threadIdx.x; i < E * 4; i += blockDim.x) masks[i] = 0u;
@@ -183,7 +182,7 @@ __global__ void __launch_bounds__(256) masks_from_topk_kernel(const int32_t* __r
     const int tl = p >> 3;
     const int t = chunk * kChunkTokens + tl;
     if (t >= T) break;
-    const int e = topk_idx[static_cast<size_t>(t) * kTopK + (p & 7)];
+    const int e = in.idx(t, p & 7);
     if (e >= kEG) record_error(status, KF_STATUS_BAD_EXPERT);
     const int le = e - offset;
     if (e >= 0 && le >= 0 && le < E) atomicOr(&masks[le * 4 + (tl >> 5)], 1u << (tl & 31));
@@ -289,7 +288,7 @@ __global__ void __launch_bounds__(kMaxLocalExperts) permute_scan_kernel(
 // the order inside an expert's segment is token order, as the reference's
 // stable argsort gives (solution/triton/kernel.py:67-69).
 __global__ void __launch_bounds__(256) permute_assign_kernel(
-    const int32_t* __restrict__ topk_idx, const float* __restrict__ topk_w, const uint4* __restrict__ chunk_masks,
+    const RowLayout in, const uint4* __restrict__ chunk_masks,
     const int32_t* __restrict__ chunk_base, const Meta* __restrict__ meta, int T, int E, int offset, int p_cap,
     int32_t* __restrict__ token_slot, int32_t* __restrict__ slot_token, float* __restrict__ slot_weight,
     int32_t* __restrict__ slot_pair, int* status) {
@@ -306,7 +305,7 @@ __global__ void __launch_bounds__(256) permute_assign_kernel(
     const int t = chunk * kChunkTokens + tl;
     if (t >= T) break;
     const size_t ti = static_cast<size_t>(t) * kTopK + (p & 7);
-    const int e = topk_idx[ti];
+    const int e = in.idx(t, p & 7);
     const int le = e - offset;
     int slot = -1;
     if (e >= 0 && le >= 0 && le < E) {
@@ -323,7 +322,7 @@ __global__ void __launch_bounds__(256) permute_assign_kernel(
         slot = -1;
       } else {
         slot_token[slot] = t;
-        slot_weight[slot] = topk_w[ti];
+        slot_weight[slot] = in.w(t, p & 7);
         slot_pair[slot] = static_cast<int32_t>(ti);
       }
     }
@@ -337,8 +336,7 @@ __global__ void __launch_bounds__(256) permute_assign_kernel(
 __global__ void __launch_bounds__(256) gather_rows_kernel(const Meta* __restrict__ meta,
                                                           const int32_t* __restrict__ tile_rows,
                                                           const int32_t* __restrict__ slot_token,
-                                                          const uint8_t* __restrict__ hidden,
-                                                          const float* __restrict__ hidden_scale, int T, int p_cap,
+                                                          const RowLayout in, int p_cap,
                                                           uint8_t* __restrict__ a_rows,
                                                           float* __restrict__ a_scale) {
   const int lane = threadIdx.x & 31;
@@ -347,15 +345,14 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const Meta* __restrict
   for (int r = blockIdx.x * warps + (threadIdx.x >> 5); r < nrows; r += gridDim.x * warps) {
     if ((r & (kBlk - 1)) >= tile_rows[r >> 7]) continue;
     const int t = slot_token[r];
-    const uint4* src = reinterpret_cast<const uint4*>(hidden + static_cast<size_t>(t) * kH);
+    const uint4* src = reinterpret_cast<const uint4*>(in.row(t));
     uint4* dst = reinterpret_cast<uint4*>(a_rows + static_cast<size_t>(r) * kH);
     uint4 v[kH / 16 / 32];
 #pragma unroll
     for (int j = 0; j < kH / 16 / 32; ++j) v[j] = src[lane + 32 * j];
 #pragma unroll
     for (int j = 0; j < kH / 16 / 32; ++j) dst[lane + 32 * j] = v[j];
-    for (int kb = lane; kb < kHB; kb += 32)
-      a_scale[static_cast<size_t>(kb) * p_cap + r] = hidden_scale[static_cast<size_t>(kb) * T + t];
+    for (int kb = lane; kb < kHB; kb += 32) a_scale[static_cast<size_t>(kb) * p_cap + r] = in.sc(t, kb);
   }
 }
 
@@ -368,9 +365,8 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const Meta* __restrict
 constexpr int kFrontThreads = 1024;
 
 __global__ void __launch_bounds__(kFrontThreads) front_small_kernel(
-    const float* __restrict__ logits, const __nv_bfloat16* __restrict__ bias, float rsf,
-    const int32_t* __restrict__ topk_in, const float* __restrict__ topk_w_in, const uint8_t* __restrict__ hidden,
-    const float* __restrict__ hidden_scale, int T, int E, int offset, int p_cap, Meta* __restrict__ meta,
+    const float* __restrict__ logits, const __nv_bfloat16* __restrict__ bias, float rsf, const RowLayout in, int T,
+    int E, int offset, int p_cap, Meta* __restrict__ meta,
     int32_t* __restrict__ tile_expert, int32_t* __restrict__ tile_row0, int32_t* __restrict__ tile_rows,
     int32_t* __restrict__ ptile_expert, int32_t* __restrict__ ptile_row0, int32_t* __restrict__ ptile_rows,
     int32_t* __restrict__ token_slot, int32_t* __restrict__ slot_token, float* __restrict__ slot_weight,
@@ -403,10 +399,10 @@ __global__ void __launch_bounds__(kFrontThreads) front_small_kernel(
     }
   } else {
     for (int p = tid; p < T * kTopK; p += kFrontThreads) {
-      const int e = topk_in[p];
+      const int e = in.idx(p >> 3, p & 7);
       if (e >= kEG) record_error(status, KF_STATUS_BAD_EXPERT);
       tk[p] = e;
-      tw[p] = topk_w_in[p];
+      tw[p] = in.w(p >> 3, p & 7);
     }
   }
   __syncthreads();
@@ -484,15 +480,14 @@ __global__ void __launch_bounds__(kFrontThreads) front_small_kernel(
   const int n = npairs;
   for (int i = warp; i < n; i += kFrontThreads / 32) {
     const int2 ts = pairs[i];
-    const uint4* src = reinterpret_cast<const uint4*>(hidden + static_cast<size_t>(ts.x) * kH);
+    const uint4* src = reinterpret_cast<const uint4*>(in.row(ts.x));
     uint4* dst = reinterpret_cast<uint4*>(a_rows + static_cast<size_t>(ts.y) * kH);
     uint4 v[kH / 16 / 32];
 #pragma unroll
     for (int j = 0; j < kH / 16 / 32; ++j) v[j] = src[lane + 32 * j];
 #pragma unroll
     for (int j = 0; j < kH / 16 / 32; ++j) dst[lane + 32 * j] = v[j];
-    for (int kb = lane; kb < kHB; kb += 32)
-      a_scale[static_cast<size_t>(kb) * p_cap + ts.y] = hidden_scale[static_cast<size_t>(kb) * T + ts.x];
+    for (int kb = lane; kb < kHB; kb += 32) a_scale[static_cast<size_t>(kb) * p_cap + ts.y] = in.sc(ts.x, kb);
   }
 }
 
@@ -561,10 +556,10 @@ cudaError_t launch_route(const float* logits, const void* bias, int T, float rsf
   return cudaGetLastError();
 }
 
-cudaError_t launch_masks_from_topk(const int32_t* topk_idx, int T, int E, int offset, uint4* chunk_masks,
-                                   int* status, cudaStream_t s) {
+cudaError_t launch_masks_from_topk(const RowLayout& in, int T, int E, int offset, uint4* chunk_masks, int* status,
+                                   cudaStream_t s) {
   const int nchunk = (T + kChunkTokens - 1) / kChunkTokens;
-  masks_from_topk_kernel<<<nchunk, 256, 0, s>>>(topk_idx, T, E, offset, chunk_masks, status);
+  masks_from_topk_kernel<<<nchunk, 256, 0, s>>>(in, T, E, offset, chunk_masks, status);
   return cudaGetLastError();
 }
 
@@ -577,24 +572,23 @@ cudaError_t launch_permute_scan(const uint4* chunk_masks, int nchunk, int E, Met
   return cudaGetLastError();
 }
 
-cudaError_t launch_permute_assign(const int32_t* topk_idx, const float* topk_w, const uint4* chunk_masks,
-                                  const int32_t* chunk_base, const Meta* meta, int T, int E, int offset, int p_cap,
-                                  int32_t* token_slot, int32_t* slot_token, float* slot_weight, int32_t* slot_pair,
-                                  int* status, cudaStream_t s) {
+cudaError_t launch_permute_assign(const RowLayout& in, const uint4* chunk_masks, const int32_t* chunk_base,
+                                  const Meta* meta, int T, int E, int offset, int p_cap, int32_t* token_slot,
+                                  int32_t* slot_token, float* slot_weight, int32_t* slot_pair, int* status,
+                                  cudaStream_t s) {
   const int nchunk = (T + kChunkTokens - 1) / kChunkTokens;
-  permute_assign_kernel<<<nchunk, 256, 0, s>>>(topk_idx, topk_w, chunk_masks, chunk_base, meta, T, E, offset, p_cap,
-                                               token_slot, slot_token, slot_weight, slot_pair, status);
+  permute_assign_kernel<<<nchunk, 256, 0, s>>>(in, chunk_masks, chunk_base, meta, T, E, offset, p_cap, token_slot,
+                                               slot_token, slot_weight, slot_pair, status);
   return cudaGetLastError();
 }
 
-cudaError_t launch_front_small(const float* logits, const void* bias, float rsf, const int32_t* topk_in,
-                               const float* topk_w_in, const uint8_t* hidden, const float* hidden_scale, int T, int E,
+cudaError_t launch_front_small(const float* logits, const void* bias, float rsf, const RowLayout& in, int T, int E,
                                int offset, int p_cap, Meta* meta, int32_t* tile_expert, int32_t* tile_row0,
                                int32_t* tile_rows, int32_t* ptile_expert, int32_t* ptile_row0, int32_t* ptile_rows,
                                int32_t* token_slot, int32_t* slot_token, float* slot_weight, int32_t* slot_pair,
                                uint8_t* a_rows, float* a_scale, int* status, cudaStream_t s) {
-  front_small_kernel<<<1, kFrontThreads, 0, s>>>(logits, static_cast<const __nv_bfloat16*>(bias), rsf, topk_in,
-                                                 topk_w_in, hidden, hidden_scale, T, E, offset, p_cap, meta,
+  front_small_kernel<<<1, kFrontThreads, 0, s>>>(logits, static_cast<const __nv_bfloat16*>(bias), rsf, in, T, E,
+                                                 offset, p_cap, meta,
                                                  tile_expert, tile_row0, tile_rows, ptile_expert, ptile_row0,
                                                  ptile_rows, token_slot, slot_token, slot_weight, slot_pair, a_rows,
                                                  a_scale, status);
@@ -602,10 +596,9 @@ cudaError_t launch_front_small(const float* logits, const void* bias, float rsf,
 }
 
 cudaError_t launch_gather_rows(const Meta* meta, const int32_t* tile_rows, const int32_t* slot_token,
-                               const uint8_t* hidden, const float* hidden_scale, int T, int p_cap, uint8_t* a_rows,
-                               float* a_scale, int grid, cudaStream_t s) {
-  gather_rows_kernel<<<grid, 256, 0, s>>>(meta, tile_rows, slot_token, hidden, hidden_scale, T, p_cap, a_rows,
-                                          a_scale);
+                               const RowLayout& in, int p_cap, uint8_t* a_rows, float* a_scale, int grid,
+                               cudaStream_t s) {
+  gather_rows_kernel<<<grid, 256, 0, s>>>(meta, tile_rows, slot_token, in, p_cap, a_rows, a_scale);
   return cudaGetLastError();
 }
 

@@ -18,7 +18,10 @@ the CUDA routing kernel, then:
 
 The collectives are ``torch.distributed`` all-to-all over NCCL (NVLink /
 NVSwitch); the split sizes are exchanged first (one small all-to-all), which
-is the one host synchronisation of a step.
+is the one host synchronisation of a step.  Dispatch (plan + packing), the
+receive side and the combine run in the library's CUDA kernels
+(``kf_ep_dispatch``, ``kf_moe_experts_packed``, ``kf_ep_combine``); the
+tensor-op functions below restate that data flow for the CPU tests.
 """
 from __future__ import annotations
 
@@ -110,7 +113,8 @@ class ExpertParallelMoE:
 
     def __init__(self, weights, local_expert_offset: int, num_local: int, group=None,
                  combine_dtype: torch.dtype = torch.bfloat16,
-                 experts_fn: Optional[Callable] = None, route_fn: Optional[Callable] = None):
+                 experts_fn: Optional[Callable] = None, route_fn: Optional[Callable] = None,
+                 plumbing: str = "cuda"):
         self.w = weights
         self.offset = int(local_expert_offset)
         self.num_local = int(num_local)
@@ -126,6 +130,12 @@ class ExpertParallelMoE:
             route_fn = route_fn or binding.route
         self.experts_fn = experts_fn
         self.route_fn = route_fn
+        # "cuda": dispatch / combine / receive-side unpacking in the library's kernels
+        # (the product path); "torch": the tensor-op restatement above, used by the
+        # CPU multi-process tests to check the data flow on gloo ranks
+        if plumbing not in ("cuda", "torch"):
+            raise ValueError("plumbing must be 'cuda' or 'torch'")
+        self.plumbing = plumbing
 
     def local_pairs(self) -> int:
         """(row, local expert) pairs this rank's expert kernels processed in the last forward (synchronises)."""
@@ -136,6 +146,32 @@ class ExpertParallelMoE:
         return int(((ids >= 0) & (loc >= 0) & (loc < self.num_local)).sum().item())
 
     def forward(self, routing_logits, routing_bias, hidden_states, hidden_states_scale, routed_scaling_factor):
+        if self.plumbing == "cuda":
+            return self._forward_cuda(routing_logits, routing_bias, hidden_states, hidden_states_scale,
+                                      routed_scaling_factor)
+        return self._forward_torch(routing_logits, routing_bias, hidden_states, hidden_states_scale,
+                                   routed_scaling_factor)
+
+    def _forward_cuda(self, routing_logits, routing_bias, hidden_states, hidden_states_scale, routed_scaling_factor):
+        from . import binding as B
+        idx, w = self.route_fn(routing_logits, routing_bias, routed_scaling_factor)
+        send, send_counts, pos = B.ep_dispatch(idx, w, hidden_states, hidden_states_scale, self.world)
+        recv_counts = _exchange_counts(send_counts, self.group)
+        s_split = send_counts.tolist()
+        r_split = recv_counts.tolist()
+        S, R = sum(s_split), sum(r_split)
+        recv = torch.empty((R, ROW_BYTES), dtype=torch.uint8, device=send.device)
+        dist.all_to_all_single(recv, send[:S], output_split_sizes=r_split, input_split_sizes=s_split,
+                               group=self.group)
+        self._last_ids = recv[:, H + HB * 4:H + HB * 4 + TOP_K * 4].contiguous().view(torch.int32)
+        part = B.experts_packed(recv, self.w.gemm1_weights, self.w.gemm1_weights_scale, self.w.gemm2_weights,
+                                self.w.gemm2_weights_scale, self.offset, out_dtype=self.combine_dtype)
+        back = torch.empty((S, H), dtype=part.dtype, device=part.device)
+        dist.all_to_all_single(back, part, output_split_sizes=s_split, input_split_sizes=r_split, group=self.group)
+        return B.ep_combine(back, pos, self.world)
+
+    def _forward_torch(self, routing_logits, routing_bias, hidden_states, hidden_states_scale,
+                       routed_scaling_factor):
         T = routing_logits.shape[0]
         idx, w = self.route_fn(routing_logits, routing_bias, routed_scaling_factor)
         plan = dispatch_plan(idx, w, self.world)

@@ -54,7 +54,7 @@ def worker(rank, world, port, T_per_rank, combine, mode, result_dir):
         ti = tokens_for(rank, T)
         layer = ep.ExpertParallelMoE(dummy_bank(E), rank * E, E,
                                      combine_dtype=torch.float32 if combine == "f32" else torch.bfloat16,
-                                     experts_fn=linear_experts, route_fn=oracle_route)
+                                     experts_fn=linear_experts, route_fn=oracle_route, plumbing="torch")
         if mode == "drop" and rank == world - 1:
             res["dropped"] = True      # leaves before its first collective
             torch.save(res, os.path.join(result_dir, f"r{rank}.pt"))
