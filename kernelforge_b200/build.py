@@ -3,7 +3,7 @@
     python -m kernelforge_b200.build [--force]
 
 Cross-compiles without a GPU.  The GEMM kernels split registers between warp
-groups with ``setmaxnreg`` (40 for the producer/MMA group, 232 for the two
+groups with ``setmaxnreg`` (48 for the producer/MMA group, 224 for the two
 epilogue groups), which is only valid when the kernel is launched with 168
 registers per thread; the build checks ptxas's report and fails otherwise.
 """

@@ -340,8 +340,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         const float2 gt = acc_g[j];
-        const float hx = (gt.x / (1.0f + expf(-gt.x))) * acc_u[j].x;
-        const float hy = (gt.y / (1.0f + expf(-gt.y))) * acc_u[j].y;
+        const float hx = silu_f(gt.x) * acc_u[j].x;
+        const float hy = silu_f(gt.y) * acc_u[j].y;
         acc_u[j] = make_float2(hx, hy);
         amax = fmaxf(amax, fmaxf(fabsf(hx), fabsf(hy)));
       }

@@ -20,6 +20,12 @@ constexpr int kIB = kI / kBlk;                // 16 K-blocks of the intermediate
 constexpr int kChunkTokens = 128;             // tokens per routing/permute chunk (4 x 32-bit masks)
 constexpr int kMaxLocalExperts = 256;
 
+// silu(x) = x * sigmoid(x) for the SwiGLU epilogues, with the hardware exp2 and
+// reciprocal approximations (a few ulp; the reference's Triton sigmoid is of the
+// same class).  Returns 0 when exp(-x) overflows, so large negative gates never
+// take a slow special-value path.
+__device__ __forceinline__ float silu_f(float x) { return x * __fdividef(1.0f, 1.0f + __expf(-x)); }
+
 // Per-call metadata written by the permute scan, read by the GEMMs and the reduce.
 struct Meta {
   int32_t num_tiles;       // row tiles of 128 permuted rows, over all local experts
