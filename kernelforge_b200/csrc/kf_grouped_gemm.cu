@@ -417,6 +417,31 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
+// In-register transpose of an 8x8 block of float4 across the 8 lanes of a lane
+// group (gl = lane & 7): on entry lane i holds v[j] = element (i, j); on exit
+// lane i holds v[j] = element (j, i).  Three butterfly stages; each exchanges
+// half of the registers with the lane gl ^ s.  The whole warp must call it.
+__device__ __forceinline__ void transpose8_f4(float4 (&v)[8], int gl) {
+#pragma unroll
+  for (int s = 4; s >= 1; s >>= 1) {
+    const bool upper = (gl & s) != 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j & s) continue;
+      const float4 send = upper ? v[j] : v[j | s];
+      float4 recv;
+      recv.x = __shfl_xor_sync(0xffffffffu, send.x, s);
+      recv.y = __shfl_xor_sync(0xffffffffu, send.y, s);
+      recv.z = __shfl_xor_sync(0xffffffffu, send.z, s);
+      recv.w = __shfl_xor_sync(0xffffffffu, send.w, s);
+      if (upper)
+        v[j] = recv;
+      else
+        v[j | s] = recv;
+    }
+  }
+}
+
 // A GEMM2 work unit as the promotion warps see it (tile entry read one unit ahead).
 struct G2Unit {
   int nb2, e, row0, nrows;
@@ -616,12 +641,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         pb.advance<2>();
       }
       if (!ok) break;
-      if (row < nrows) {
-        const float w = g.slot_weight[row0 + row];
-        float4* dst = reinterpret_cast<float4*>(g.y + static_cast<size_t>(row0 + row) * kH + nb2 * 256 + h * 128);
+      if (live) {
+        // Each lane holds one row's 128 columns.  Stored lane-per-row, every
+        // 16-byte store of a warp lands in a different row (32 scattered
+        // sectors per instruction).  An 8x8 transpose of float4s inside each
+        // group of 8 lanes turns that into lane-per-column, so one store
+        // instruction writes four whole 128-byte row segments.
+        const float w = row < nrows ? g.slot_weight[row0 + row] : 0.f;
+        const int gl = lane & 7;
+        const int r_base = q * 32 + (lane & ~7);  // first row of this lane's group
+        float* ybase = g.y + static_cast<size_t>(row0) * kH + nb2 * 256 + h * 128;
 #pragma unroll
-        for (int j = 0; j < 64; j += 2)
-          dst[j / 2] = make_float4(acc[j].x * w, acc[j].y * w, acc[j + 1].x * w, acc[j + 1].y * w);
+        for (int m = 0; m < 4; ++m) {
+          float4 v[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float2 p0 = acc[16 * m + 2 * j], p1 = acc[16 * m + 2 * j + 1];
+            v[j] = make_float4(p0.x * w, p0.y * w, p1.x * w, p1.y * w);
+          }
+          transpose8_f4(v, gl);
+          // v[j] = float4 (8m + gl) of row r_base + j
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int r = r_base + j;
+            if (r < nrows) reinterpret_cast<float4*>(ybase + static_cast<size_t>(r) * kH)[8 * m + gl] = v[j];
+          }
+        }
       }
       cur = nxt;
     }
