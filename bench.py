@@ -285,38 +285,74 @@ def main():
     ms_per_step = ms / args.steps
     value = world * T * args.steps / (ms / 1e3)
 
-    # end to end through the public API: per-step inputs from pinned host memory, result back to host
+    # End to end through the public API: every step copies its inputs from pinned
+    # host memory and its bf16 result back to pinned host memory.  As in a serving
+    # loop, the copies run on their own streams and overlap the neighbouring
+    # steps' kernels: step k+1's inputs go up and step k-1's result comes down
+    # while step k computes (two device input sets, two host output buffers).
     e2e = None
-    h_logits = ti.routing_logits.cpu().pin_memory()
-    h_bias = ti.routing_bias.cpu().pin_memory()
-    h_hid = ti.hidden_states.cpu().pin_memory()
-    h_hs = ti.hidden_states_scale.cpu().pin_memory()
-    h_out = torch.empty((T, H), dtype=torch.bfloat16).pin_memory()
-    d_logits, d_bias = torch.empty_like(ti.routing_logits), torch.empty_like(ti.routing_bias)
-    d_hid, d_hs = torch.empty_like(ti.hidden_states), torch.empty_like(ti.hidden_states_scale)
-    h2d = sum(t.numel() * t.element_size() for t in (h_logits, h_bias, h_hid, h_hs))
-    d2h = h_out.numel() * h_out.element_size()
+    h_in = [tuple(t.cpu().pin_memory() for t in (ti.routing_logits, ti.routing_bias, ti.hidden_states,
+                                                  ti.hidden_states_scale)) for _ in range(2)]
+    h_out = [torch.empty((T, H), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    d_in = [tuple(torch.empty_like(t) for t in (ti.routing_logits, ti.routing_bias, ti.hidden_states,
+                                                  ti.hidden_states_scale)) for _ in range(2)]
+    h2d = sum(t.numel() * t.element_size() for t in h_in[0])
+    d2h = h_out[0].numel() * h_out[0].element_size()
     e2e_steps = max(3, min(args.steps, 20))
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev = lambda: torch.cuda.Event(enable_timing=False)
+    loaded = [ev() for _ in range(e2e_steps)]
+    computed = [ev() for _ in range(e2e_steps)]
+
+    def upload(k):
+        b = k % 2
+        if k >= 2:
+            up.wait_event(computed[k - 2])      # step k-2 has finished reading this input set
+        with torch.cuda.stream(up):
+            for d, h in zip(d_in[b], h_in[b]):
+                d.copy_(h, non_blocking=True)
+        loaded[k].record(up)
+
     barrier()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        d_logits.copy_(h_logits, non_blocking=True)
-        d_bias.copy_(h_bias, non_blocking=True)
-        d_hid.copy_(h_hid, non_blocking=True)
-        d_hs.copy_(h_hs, non_blocking=True)
-        o = step(d_logits, d_bias, d_hid, d_hs)
-        h_out.copy_(o, non_blocking=True)
-    e1.record(stream)
+    e0.record(up)
+    stream.wait_event(e0)
+    down.wait_event(e0)
+    upload(0)
+    for k in range(e2e_steps):
+        if k + 1 < e2e_steps:
+            upload(k + 1)
+        stream.wait_event(loaded[k])
+        if args.graph and world == 1:
+            stream.wait_stream(down)   # the graph reuses one output buffer: step k-1's copy must be done
+        o = step(*d_in[k % 2])
+        computed[k].record(stream)
+        down.wait_event(computed[k])
+        o.record_stream(down)
+        with torch.cuda.stream(down):
+            h_out[k % 2].copy_(o, non_blocking=True)
+    down.wait_stream(stream)
+    down.wait_stream(up)
+    e1.record(down)
     torch.cuda.synchronize(dev)
     e_ms = e0.elapsed_time(e1)
     if world > 1:
         t = torch.tensor([e_ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         e_ms = float(t.item())
+    # the copies alone, serialised, for one step (how much the overlap hides)
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    c0.record(stream)
+    for d, h in zip(d_in[0], h_in[0]):
+        d.copy_(h, non_blocking=True)
+    h_out[0].copy_(o, non_blocking=True)
+    c1.record(stream)
+    torch.cuda.synchronize(dev)
     e2e = {"value": world * T * e2e_steps / (e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-           "d2h_bytes_per_step": d2h, "steps": e2e_steps}
+           "d2h_bytes_per_step": d2h, "steps": e2e_steps, "copy_ms_per_step_serial": c0.elapsed_time(c1),
+           "overlap": "each step's host copies run on side streams beside the neighbouring steps' kernels"}
 
     # roofline of the dominant kernel (GEMM1: 2/3 of the layer's FLOPs)
     g1_ms, g1_n = prof["gemm1_swiglu"]
