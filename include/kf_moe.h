@@ -16,6 +16,8 @@
  *                      grouped GEMM2 + index_add combine  (_sort_tokens :46-82,
  *                                                          _launch_grouped_gemm1_swiglu :626,
  *                                                          _launch_grouped_gemm2 :688)
+ *   kf_quantize_hidden <- _quantize_fp8_block_rows        kernel.py:126-141
+ *                      (the FP8 format of hidden_states / hidden_states_scale)
  *
  * All pointers are device pointers (except where noted), all tensors are dense
  * row-major, and every call is asynchronous on `stream` (a cudaStream_t, NULL =
@@ -152,6 +154,16 @@ int kf_ep_dispatch(const int32_t* topk_idx, const float* topk_weight, const void
  */
 int kf_ep_combine(const void* partials, int32_t partials_fp32, const int32_t* pos, int32_t num_tokens,
                   int32_t world, void* output, void* stream);
+
+/*
+ * FP8 block quantisation of bf16 rows into the layer's input format (the step
+ * before kf_moe_forward): x bf16 [T, 7168] -> out e4m3 [T, 7168] and out_scale
+ * f32 [56, T] (K-block major, as hidden_states_scale), per row and 128 columns
+ * scale = absmax / 448 (1 for an all-zero block), out = e4m3(x / scale) rounded
+ * to nearest even.  x and out must be 16-byte aligned.  Inputs holding NaN or
+ * infinity are outside the contract (the block maximum skips NaN).
+ */
+int kf_quantize_hidden(const void* x, int32_t num_tokens, void* out, float* out_scale, void* stream);
 
 /*
  * Synchronises `stream`, then copies the device status word of the last call

@@ -68,6 +68,8 @@ def _load():
         lib.kf_ep_dispatch.argtypes = [vp, vp, vp, vp, i32, i32, vp, vp, vp, vp, sz, vp]
         lib.kf_ep_combine.restype = ctypes.c_int
         lib.kf_ep_combine.argtypes = [vp, i32, vp, i32, i32, vp, vp]
+        lib.kf_quantize_hidden.restype = ctypes.c_int
+        lib.kf_quantize_hidden.argtypes = [vp, i32, vp, vp, vp]
         lib.kf_moe_profile_begin.restype = ctypes.c_int
         lib.kf_moe_profile_begin.argtypes = []
         lib.kf_moe_profile_end.restype = ctypes.c_int
@@ -324,3 +326,21 @@ def ep_combine(partials, pos, world: int):
                                ctypes.c_void_p(stream.cuda_stream))
     _check(rc, "kf_ep_combine")
     return out
+
+
+def quantize_hidden(x: torch.Tensor):
+    """bf16 rows ``[T, 7168]`` -> (e4m3 ``[T, 7168]``, f32 scales ``[56, T]``): the input format of ``kernel``.
+
+    Per row and 128 columns: scale = absmax / 448 (1 for an all-zero block),
+    q = e4m3(x / scale) -- the reference's ``_quantize_fp8_block_rows``
+    (``solution/triton/kernel.py:126-141``), computed by ``kf_quantize_hidden``.
+    """
+    if x.dim() != 2 or x.shape[1] != H or x.dtype != torch.bfloat16 or not x.is_cuda:
+        raise RuntimeError("quantize_hidden expects a CUDA bf16 tensor [T, 7168]")
+    x = x.contiguous()
+    T = x.shape[0]
+    q = torch.empty((T, H), dtype=torch.float8_e4m3fn, device=x.device)
+    s = torch.empty((H // 128, T), dtype=torch.float32, device=x.device)
+    rc = _load().kf_quantize_hidden(_ptr(x), T, _ptr(q), _ptr(s), torch.cuda.current_stream(x.device).cuda_stream)
+    _check(rc, "kf_quantize_hidden")
+    return q, s

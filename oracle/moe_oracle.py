@@ -16,6 +16,9 @@ Reference (chinmay29/kernelforge), all in ``solution/triton/kernel.py``:
   that runs with ``KF_USE_GROUPED_TRITON=0``)
 * SwiGLU ............. ``silu(X2) * X1`` with X1 = W13 rows [0, I) and X2 = rows
   [I, 2I) (lines 1940-1943)
+* row quantisation ... ``_quantize_fp8_block_rows`` lines 126-141 (the FP8
+  format of ``hidden_states`` / ``hidden_states_scale``: per row and 128
+  columns, scale = absmax / 448, or 1 for an all-zero block)
 
 Pinning: ``tests/golden/make_golden.py`` imports the reference ``kernel`` in the
 build container and records its outputs on seeded inputs; ``tests/test_oracle.py``
@@ -87,6 +90,20 @@ def sort_tokens(topk_idx: torch.Tensor, local_start: int, num_local: int):
     if num_local > 1:
         starts[1:] = torch.cumsum(counts, 0)[:-1]
     return sorted_ids, sorted_le, starts, counts
+
+
+def quantize_rows_per_128(x: torch.Tensor):
+    """``kernel.py:126-141``: ``[R, K]`` -> e4m3 ``[R, K]`` and fp32 scales ``[K/128, R]``.
+
+    absmax over each 128-wide block; scale = absmax / 448 (1 where absmax is 0);
+    q = e4m3(x / scale) with torch's round-to-nearest cast.
+    """
+    r, k = x.shape
+    blocks = x.to(torch.float32).view(r, k // BLOCK, BLOCK)
+    absmax = blocks.abs().amax(dim=2)
+    scale = torch.where(absmax > 0, absmax / torch.finfo(torch.float8_e4m3fn).max, torch.ones_like(absmax))
+    q = (blocks / scale.unsqueeze(-1)).to(torch.float8_e4m3fn).reshape(r, k)
+    return q.contiguous(), scale.t().contiguous()
 
 
 def dequant_hidden_rows(hidden_states, hidden_states_scale, token_ids):

@@ -50,3 +50,20 @@ def test_tolerance_checker_rejects_single_fp8_requant_scale_error():
     bad = (ref.float() * 1.05).to(torch.bfloat16)
     assert not O.check_tolerance(bad, ref)["ok"]
     assert O.check_tolerance(ref, ref)["ok"]
+
+
+def _quant_golden():
+    import os
+    d = np.load(os.path.join(os.path.dirname(__file__), "golden", "quant_golden.npz"))
+    x = torch.from_numpy(d["x_bits"].view(np.int16)).view(torch.bfloat16)
+    return x, torch.from_numpy(d["q_bits"]), torch.from_numpy(d["scale"])
+
+
+def test_oracle_quantizer_matches_reference_bit_exact():
+    """``quantize_rows_per_128`` against the reference ``_quantize_fp8_block_rows`` outputs (kernel.py:126-141)."""
+    x, q_ref, s_ref = _quant_golden()
+    q, s = O.quantize_rows_per_128(x)
+    assert torch.equal(q.view(torch.uint8), q_ref)
+    assert torch.equal(s, s_ref)
+    assert torch.equal(s[:, 6], torch.ones(56))       # all-zero row: scale 1, codes 0
+    assert int(q[6].view(torch.uint8).max()) == 0
