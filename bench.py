@@ -363,8 +363,13 @@ def main():
         g1_avg = g1_ms / g1_n
         achieved = GEMM1_FLOP_PER_PAIR * pairs / (g1_avg / 1e3) / 1e12
         peak = 2.0 * peaks["bf16_sustained"]
+        # DRAM bytes of one GEMM1 launch from an ncu capture of this exact workload (N = 1, 256 local
+        # experts, T = 8192): profiles/launches_ep_layer_T8192.md.  Other workloads: not captured.
+        traffic = 12.01e9 if (args.workload == "ep" and world == 1 and T == 8192) else None
         roofline = {"bound": "tensor", "kernel": "gemm1_swiglu", "achieved": achieved, "peak": peak,
-                    "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                    "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+                    "traffic_note": "DRAM bytes per launch (ncu dram__bytes_read+write); algorithmic 8.26e9"
+                                    if traffic else None,
                     "peak_note": f"FP8 dense = 2 x {peaks['source']} sustained cuBLAS bf16 "
                                  f"({peaks['bf16_sustained']} TFLOP/s)",
                     "avg_launch_ms": g1_avg}
