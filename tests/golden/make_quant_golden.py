@@ -1,9 +1,10 @@
 """Golden vectors for the hidden-state FP8 quantiser, from the REFERENCE function.
 
-Run in the build container only (imports ``_quantize_fp8_block_rows`` from
-``/root/reference/solution/triton/kernel.py``, lines 126-141, on CPU):
+Run where a checkout of the reference (chinmay29/kernelforge) is available; it
+imports ``_quantize_fp8_block_rows`` (``solution/triton/kernel.py`` lines 126-141)
+from that checkout and runs it on CPU:
 
-    python tests/golden/make_quant_golden.py
+    python tests/golden/make_quant_golden.py <reference checkout>
 
 Writes ``tests/golden/quant_golden.npz``: bf16 inputs (as uint16 bits), the
 reference's e4m3 output (as uint8 bits) and its ``[56, R]`` fp32 scales, for
@@ -15,12 +16,13 @@ from __future__ import annotations
 
 import importlib.util
 import os
+import sys
 
 import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF_KERNEL = "/root/reference/solution/triton/kernel.py"
+REF_KERNEL = os.path.join(sys.argv[1] if len(sys.argv) > 1 else ".", "solution", "triton", "kernel.py")
 H = 7168
 
 
