@@ -53,6 +53,8 @@ def parse():
     p.add_argument("--tokens", type=int, default=None)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--graph", action="store_true", help="replay the layer as a CUDA graph (1 GPU)")
+    p.add_argument("--ep-exchange", default="p2p", choices=["p2p", "nccl"],
+                   help="N > 1: peer-to-peer stores into symmetric buffers, or NCCL all-to-all")
     return p.parse_args()
 
 
@@ -220,7 +222,7 @@ def main():
 
     if world > 1:
         from kernelforge_b200 import ep
-        layer = ep.ExpertParallelMoE(wb, offset, E)
+        layer = ep.ExpertParallelMoE(wb, offset, E, plumbing="p2p" if args.ep_exchange == "p2p" else "cuda")
 
         def step(logits, bias, hid, hs):
             return layer.forward(logits, bias, hid, hs, 2.5)
@@ -391,7 +393,8 @@ def main():
             "vs_baseline": None, "dtype": "fp8_e4m3 (fp32 accumulate)", "data": "synthetic",
             "config": {"workload": name, "tokens_per_gpu": T, "local_experts_per_gpu": E,
                        "global_experts": E_GLOBAL, "hidden": H, "intermediate": I, "top_k": 8,
-                       "parallelism": f"ep{world}", "l2": "inputs larger than L2 (weights stream from HBM)",
+                       "parallelism": f"ep{world}", "ep_exchange": args.ep_exchange if world > 1 else None,
+                       "l2": "inputs larger than L2 (weights stream from HBM)",
                        "pairs_rank0": pairs, "cuda_graph": bool(args.graph and world == 1)},
             "p50_step_ms": step_ms[len(step_ms) // 2], "p90_step_ms": step_ms[int(len(step_ms) * 0.9)],
             "tflops_per_gpu": (FLOP_PER_PAIR * pairs / (ms_per_step / 1e3) / 1e12) if pairs else None,

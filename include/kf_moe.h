@@ -60,6 +60,7 @@ extern "C" {
 #define KF_STATUS_TIMEOUT_EPILOGUE 0x04 /* a promotion/epilogue warp waited too long */
 #define KF_STATUS_BAD_EXPERT 0x08       /* a routed expert id outside [0, 256) */
 #define KF_STATUS_SLOT_OVERFLOW 0x10    /* a permuted row index beyond the workspace capacity */
+#define KF_STATUS_TIMEOUT_PEER 0x20     /* a peer rank did not reach kf_ep_barrier in time */
 
 /*
  * Bytes of scratch memory a call with `num_tokens` tokens and `num_local_experts`
@@ -152,6 +153,50 @@ int kf_ep_dispatch(const int32_t* topk_idx, const float* topk_weight, const void
  * in ascending order of partials[pos[t, d]] (rows of bf16, or f32 when
  * partials_fp32), accumulated in f32 and rounded once.
  */
+/*
+ * Expert-parallel exchange over peer memory (NVLink / NVSwitch), replacing the
+ * two NCCL all-to-alls of the dispatch / combine above with stores into the
+ * ranks' symmetric buffers (one allocation per rank at the same layout, mapped
+ * into every peer).  Arrays named peer_* are DEVICE arrays of `world` device
+ * pointers, entry q pointing into rank q's buffer.  A step, on every rank:
+ *
+ *   kf_ep_plan_p2p    masks + scan (as kf_ep_dispatch) and publishes this rank's
+ *                     per-destination row counts as row `rank` of every rank's
+ *                     [world][world] int32 count matrix (peer_counts)
+ *   kf_ep_barrier     all count rows have landed
+ *   kf_ep_pack_p2p    packs each (token, destination) row (kf_ep_dispatch's
+ *                     format) straight into rank d's receive buffer (peer_recv),
+ *                     sources in rank order, and writes pos as kf_ep_dispatch
+ *   kf_ep_barrier     all rows have landed; this rank received
+ *                     sum over s of counts[s][rank] rows
+ *   (kf_moe_experts_packed on the received rows -> bf16 partials)
+ *   kf_ep_return_p2p  sends each partial row back into its source's return
+ *                     buffer (peer_back) at the row's position in the source's
+ *                     send order
+ *   kf_ep_barrier     all partials have landed; kf_ep_combine(return buffer, pos)
+ *
+ * All ranks pass the same num_tokens; each receive buffer holds recv_capacity
+ * = num_tokens * world rows (a row beyond it is dropped and sets
+ * KF_STATUS_SLOT_OVERFLOW in *status).  counts is this rank's own (complete)
+ * count matrix.  The barrier stores `epoch`
+ * (one more than the previous barrier's) into slot `rank` of every rank's int32
+ * flag array (peer_flags; zeroed before the first barrier) and waits, bounded,
+ * until its own flags (my_flags) all reach it; a rank that does not arrive sets
+ * KF_STATUS_TIMEOUT_PEER in *status (device int) instead of hanging.  The
+ * reference has no multi-GPU path (the layer's data contract carries
+ * local_expert_offset, kernel.py:1826).
+ */
+int kf_ep_plan_p2p(const int32_t* topk_idx, int32_t num_tokens, int32_t world, int32_t rank,
+                   int32_t* const* peer_counts, void* workspace, size_t workspace_bytes, void* stream);
+int kf_ep_pack_p2p(const int32_t* topk_idx, const float* topk_weight, const void* hidden_states,
+                   const float* hidden_states_scale, int32_t num_tokens, int32_t world, int32_t rank,
+                   const int32_t* counts, uint8_t* const* peer_recv, int32_t recv_capacity, int32_t* pos,
+                   int32_t* status, void* workspace, size_t workspace_bytes, void* stream);
+int kf_ep_return_p2p(const void* partials, int32_t num_rows, int32_t world, int32_t rank, const int32_t* counts,
+                     void* const* peer_back, void* stream);
+int kf_ep_barrier(int32_t* const* peer_flags, const int32_t* my_flags, int32_t rank, int32_t world, int32_t epoch,
+                  int32_t* status, void* stream);
+
 int kf_ep_combine(const void* partials, int32_t partials_fp32, const int32_t* pos, int32_t num_tokens,
                   int32_t world, void* output, void* stream);
 

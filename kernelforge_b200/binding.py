@@ -68,6 +68,14 @@ def _load():
         lib.kf_ep_dispatch.argtypes = [vp, vp, vp, vp, i32, i32, vp, vp, vp, vp, sz, vp]
         lib.kf_ep_combine.restype = ctypes.c_int
         lib.kf_ep_combine.argtypes = [vp, i32, vp, i32, i32, vp, vp]
+        lib.kf_ep_plan_p2p.restype = ctypes.c_int
+        lib.kf_ep_plan_p2p.argtypes = [vp, i32, i32, i32, vp, vp, sz, vp]
+        lib.kf_ep_pack_p2p.restype = ctypes.c_int
+        lib.kf_ep_pack_p2p.argtypes = [vp, vp, vp, vp, i32, i32, i32, vp, vp, i32, vp, vp, vp, sz, vp]
+        lib.kf_ep_return_p2p.restype = ctypes.c_int
+        lib.kf_ep_return_p2p.argtypes = [vp, i32, i32, i32, vp, vp, vp]
+        lib.kf_ep_barrier.restype = ctypes.c_int
+        lib.kf_ep_barrier.argtypes = [vp, vp, i32, i32, i32, vp, vp]
         lib.kf_quantize_hidden.restype = ctypes.c_int
         lib.kf_quantize_hidden.argtypes = [vp, i32, vp, vp, vp]
         lib.kf_moe_profile_begin.restype = ctypes.c_int
@@ -282,6 +290,17 @@ def experts_packed(rows, gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm
 
 
 _ep_ws: dict = {}
+
+
+def _ep_workspace(device: torch.device, need: int) -> torch.Tensor:
+    """Cached scratch of the expert-parallel kernels for (device, current stream)."""
+    stream = torch.cuda.current_stream(device)
+    key = (device.index, stream.cuda_stream)
+    buf = _ep_ws.get(key)
+    if buf is None or buf.numel() < need:
+        buf = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
+        _ep_ws[key] = buf
+    return buf
 
 
 def ep_dispatch(topk_idx, topk_weight, hidden_states, hidden_states_scale, world: int):

@@ -69,10 +69,15 @@ __global__ void __launch_bounds__(256) ep_masks_kernel(const int32_t* __restrict
     dmasks[static_cast<size_t>(chunk) * world + d] = make_uint4(m[d * 4], m[d * 4 + 1], m[d * 4 + 2], m[d * 4 + 3]);
 }
 
+// peer_counts (peer-to-peer mode only): device array of `world` pointers to each
+// rank's [world][world] count matrix; this rank's row `rank` is written into all
+// of them (plain stores over NVLink, made visible system-wide before the kernel
+// ends).
 __global__ void __launch_bounds__(kMaxRanks) ep_scan_kernel(const uint4* __restrict__ dmasks, int nchunk, int world,
                                                             int32_t* __restrict__ chunk_base,
                                                             int64_t* __restrict__ send_counts,
-                                                            int32_t* __restrict__ dest_offset) {
+                                                            int32_t* __restrict__ dest_offset,
+                                                            int32_t* const* __restrict__ peer_counts, int rank) {
   __shared__ int32_t tot[kMaxRanks];
   const int d = threadIdx.x;
   if (d < world) {
@@ -82,7 +87,11 @@ __global__ void __launch_bounds__(kMaxRanks) ep_scan_kernel(const uint4* __restr
       run += popc4(dmasks[static_cast<size_t>(c) * world + d]);
     }
     tot[d] = run;
-    send_counts[d] = run;
+    if (send_counts) send_counts[d] = run;
+    if (peer_counts) {
+      for (int q = 0; q < world; ++q) peer_counts[q][rank * world + d] = run;
+      __threadfence_system();
+    }
   }
   __syncthreads();
   if (d == 0) {
@@ -100,15 +109,26 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const int32_t* __restrict_
                                                       const uint4* __restrict__ dmasks,
                                                       const int32_t* __restrict__ chunk_base,
                                                       const int32_t* __restrict__ dest_offset,
-                                                      uint8_t* __restrict__ send_rows, int32_t* __restrict__ pos) {
+                                                      uint8_t* __restrict__ send_rows, int32_t* __restrict__ pos,
+                                                      uint8_t* const* __restrict__ peer_recv,
+                                                      const int32_t* __restrict__ counts, int rank, int recv_cap,
+                                                      int* __restrict__ status) {
   __shared__ uint4 m[kMaxRanks];
   __shared__ int32_t base[kMaxRanks];
+  __shared__ int32_t pbase[kMaxRanks];
   __shared__ int2 rows[kChunkTokens * kMaxDestPerToken];
   __shared__ int nrows;
   const int chunk = blockIdx.x;
   for (int d = threadIdx.x; d < world; d += blockDim.x) {
     m[d] = dmasks[static_cast<size_t>(chunk) * world + d];
-    base[d] = dest_offset[d] + chunk_base[static_cast<size_t>(chunk) * world + d];
+    const int cb = chunk_base[static_cast<size_t>(chunk) * world + d];
+    base[d] = dest_offset[d] + cb;
+    if (peer_recv) {
+      // rank d's receive buffer holds the rows of sources 0, 1, ... in order
+      int off = 0;
+      for (int s = 0; s < rank; ++s) off += counts[s * world + d];
+      pbase[d] = off + cb;
+    }
   }
   if (threadIdx.x == 0) nrows = 0;
   __syncthreads();
@@ -123,7 +143,7 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const int32_t* __restrict_
       int r = __popc(word(md, w) & ((1u << (tl & 31)) - 1u));
       for (int k = 0; k < w; ++k) r += __popc(word(md, k));
       slot = base[d] + r;
-      rows[atomicAdd(&nrows, 1)] = make_int2(t * kMaxRanks + d, slot);
+      rows[atomicAdd(&nrows, 1)] = make_int2(t * kMaxRanks + d, peer_recv ? pbase[d] + r : slot);
     }
     pos[static_cast<size_t>(t) * world + d] = slot;
   }
@@ -133,7 +153,11 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const int32_t* __restrict_
   for (int i = warp; i < n; i += blockDim.x / 32) {
     const int2 r = rows[i];
     const int t = r.x / kMaxRanks, d = r.x % kMaxRanks;
-    uint8_t* dst = send_rows + static_cast<size_t>(r.y) * kPackedRowBytes;
+    if (peer_recv && r.y >= recv_cap) {  // the ranks disagree on the token count: drop, report
+      if (lane == 0) atomicOr(status, KF_STATUS_SLOT_OVERFLOW);
+      continue;
+    }
+    uint8_t* dst = (peer_recv ? peer_recv[d] : send_rows) + static_cast<size_t>(r.y) * kPackedRowBytes;
     const uint4* src = reinterpret_cast<const uint4*>(hidden + static_cast<size_t>(t) * kH);
     uint4 v[kH / 16 / 32];
 #pragma unroll
@@ -150,6 +174,68 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const int32_t* __restrict_
           own ? topk_w[static_cast<size_t>(t) * kTopK + lane] : 0.f;
     }
   }
+  if (peer_recv) __threadfence_system();
+}
+
+// Peer-to-peer return of the expert partials: received row r came from the
+// source s whose block holds it (sources in rank order) and is that source's
+// j-th row for this rank; it goes to row (s's rows for ranks below this one) + j
+// of s's return buffer, i.e. back to the position the row had in s's send order.
+// One warp per row, 16-byte stores over NVLink.
+__global__ void __launch_bounds__(256) ep_return_kernel(const __nv_bfloat16* __restrict__ partials, int R, int world,
+                                                        int rank, const int32_t* __restrict__ counts,
+                                                        __nv_bfloat16* const* __restrict__ peer_back) {
+  __shared__ int32_t recv_off[kMaxRanks + 1];
+  __shared__ int32_t send_off[kMaxRanks];
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int s = 0; s < world; ++s) {
+      recv_off[s] = acc;
+      acc += counts[s * world + rank];
+      int so = 0;
+      for (int d = 0; d < rank; ++d) so += counts[s * world + d];
+      send_off[s] = so;
+    }
+    recv_off[world] = acc;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < R; r += warps) {
+    int s = 0;
+    while (s + 1 < world && recv_off[s + 1] <= r) ++s;
+    const size_t dst_row = static_cast<size_t>(send_off[s]) + (r - recv_off[s]);
+    const uint4* src = reinterpret_cast<const uint4*>(partials + static_cast<size_t>(r) * kH);
+    uint4* dst = reinterpret_cast<uint4*>(peer_back[s] + dst_row * kH);
+#pragma unroll 4
+    for (int i = lane; i < kH * 2 / 16; i += 32) dst[i] = src[i];
+  }
+  __threadfence_system();
+}
+
+// Barrier over the ranks' symmetric flag arrays: thread q stores `epoch` into
+// slot `rank` of rank q's flags (after a system-scope fence, so every earlier
+// peer store of this stream is visible first), then waits until slot q of this
+// rank's flags reaches `epoch`.  Bounded: after kWaitCycles it records
+// KF_STATUS_TIMEOUT_PEER and returns.  Epochs grow by one per barrier.
+__global__ void __launch_bounds__(kMaxRanks) ep_barrier_kernel(int32_t* const* __restrict__ peer_flags,
+                                                               const int32_t* __restrict__ my_flags, int rank,
+                                                               int world, int epoch, int* __restrict__ status) {
+  const int q = threadIdx.x;
+  if (q >= world) return;
+  __threadfence_system();
+  asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(peer_flags[q] + rank), "r"(epoch) : "memory");
+  const long long t0 = clock64();
+  while (true) {
+    int v;
+    asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(my_flags + q) : "memory");
+    if (v - epoch >= 0) break;
+    if (clock64() - t0 > kWaitCycles) {
+      atomicOr(status, KF_STATUS_TIMEOUT_PEER);
+      break;
+    }
+  }
+  __threadfence_system();
 }
 
 __global__ void __launch_bounds__(256) ep_combine_kernel(const void* __restrict__ partials, int fp32,
@@ -228,10 +314,71 @@ int kf_ep_dispatch(const int32_t* topk_idx, const float* topk_weight, const void
   int32_t* dest_offset = ws_ptr<int32_t>(workspace, w.dest_offset);
   const int per_rank = kEG / world;
   ep_masks_kernel<<<nchunk, 256, 0, s>>>(topk_idx, T, per_rank, world, dmasks);
-  ep_scan_kernel<<<1, kMaxRanks, 0, s>>>(dmasks, nchunk, world, chunk_base, send_counts, dest_offset);
+  ep_scan_kernel<<<1, kMaxRanks, 0, s>>>(dmasks, nchunk, world, chunk_base, send_counts, dest_offset, nullptr, 0);
   ep_pack_kernel<<<nchunk, 256, 0, s>>>(topk_idx, topk_weight, static_cast<const uint8_t*>(hidden_states),
                                         hidden_states_scale, T, per_rank, world, dmasks, chunk_base, dest_offset,
-                                        static_cast<uint8_t*>(send_rows), pos);
+                                        static_cast<uint8_t*>(send_rows), pos, nullptr, nullptr, 0, 0, nullptr);
+  return cudaGetLastError() == cudaSuccess ? KF_OK : KF_ERR_CUDA;
+}
+
+int kf_ep_plan_p2p(const int32_t* topk_idx, int32_t num_tokens, int32_t world, int32_t rank,
+                   int32_t* const* peer_counts, void* workspace, size_t workspace_bytes, void* stream) {
+  const int T = num_tokens;
+  if (T < 0 || !valid_world(world) || rank < 0 || rank >= world || !peer_counts || !workspace)
+    return KF_ERR_INVALID_ARGUMENT;
+  if (T > 0 && !topk_idx) return KF_ERR_INVALID_ARGUMENT;
+  const EpWorkspace w = plan_ep(T, world);
+  if (workspace_bytes < w.total) return KF_ERR_WORKSPACE_TOO_SMALL;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int nchunk = (T + kChunkTokens - 1) / kChunkTokens;
+  uint4* dmasks = ws_ptr<uint4>(workspace, w.dmasks);
+  if (nchunk > 0) ep_masks_kernel<<<nchunk, 256, 0, s>>>(topk_idx, T, kEG / world, world, dmasks);
+  // with no tokens the scan still publishes a row of zeros: the peers wait for it
+  ep_scan_kernel<<<1, kMaxRanks, 0, s>>>(dmasks, nchunk, world, ws_ptr<int32_t>(workspace, w.chunk_base), nullptr,
+                                         ws_ptr<int32_t>(workspace, w.dest_offset), peer_counts, rank);
+  return cudaGetLastError() == cudaSuccess ? KF_OK : KF_ERR_CUDA;
+}
+
+int kf_ep_pack_p2p(const int32_t* topk_idx, const float* topk_weight, const void* hidden_states,
+                   const float* hidden_states_scale, int32_t num_tokens, int32_t world, int32_t rank,
+                   const int32_t* counts, uint8_t* const* peer_recv, int32_t recv_capacity, int32_t* pos,
+                   int32_t* status, void* workspace, size_t workspace_bytes, void* stream) {
+  const int T = num_tokens;
+  if (T < 0 || !valid_world(world) || rank < 0 || rank >= world) return KF_ERR_INVALID_ARGUMENT;
+  if (T == 0) return KF_OK;
+  if (!topk_idx || !topk_weight || !hidden_states || !hidden_states_scale || !counts || !peer_recv || !pos ||
+      !status || !workspace || recv_capacity < 0)
+    return KF_ERR_INVALID_ARGUMENT;
+  if (reinterpret_cast<uintptr_t>(hidden_states) & 15u) return KF_ERR_INVALID_ARGUMENT;
+  const EpWorkspace w = plan_ep(T, world);
+  if (workspace_bytes < w.total) return KF_ERR_WORKSPACE_TOO_SMALL;
+  const int nchunk = (T + kChunkTokens - 1) / kChunkTokens;
+  ep_pack_kernel<<<nchunk, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      topk_idx, topk_weight, static_cast<const uint8_t*>(hidden_states), hidden_states_scale, T, kEG / world, world,
+      ws_ptr<uint4>(workspace, w.dmasks), ws_ptr<int32_t>(workspace, w.chunk_base),
+      ws_ptr<int32_t>(workspace, w.dest_offset), nullptr, pos, peer_recv, counts, rank, recv_capacity, status);
+  return cudaGetLastError() == cudaSuccess ? KF_OK : KF_ERR_CUDA;
+}
+
+int kf_ep_return_p2p(const void* partials, int32_t num_rows, int32_t world, int32_t rank, const int32_t* counts,
+                     void* const* peer_back, void* stream) {
+  if (num_rows < 0 || !valid_world(world) || rank < 0 || rank >= world) return KF_ERR_INVALID_ARGUMENT;
+  if (num_rows == 0) return KF_OK;
+  if (!partials || !counts || !peer_back || (reinterpret_cast<uintptr_t>(partials) & 15u))
+    return KF_ERR_INVALID_ARGUMENT;
+  const int blocks = (num_rows + 7) / 8 < 4 * 148 ? (num_rows + 7) / 8 : 4 * 148;
+  ep_return_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(partials), num_rows, world, rank, counts,
+      reinterpret_cast<__nv_bfloat16* const*>(peer_back));
+  return cudaGetLastError() == cudaSuccess ? KF_OK : KF_ERR_CUDA;
+}
+
+int kf_ep_barrier(int32_t* const* peer_flags, const int32_t* my_flags, int32_t rank, int32_t world, int32_t epoch,
+                  int32_t* status, void* stream) {
+  if (!valid_world(world) || rank < 0 || rank >= world || !peer_flags || !my_flags || !status)
+    return KF_ERR_INVALID_ARGUMENT;
+  ep_barrier_kernel<<<1, kMaxRanks, 0, static_cast<cudaStream_t>(stream)>>>(peer_flags, my_flags, rank, world, epoch,
+                                                                           status);
   return cudaGetLastError() == cudaSuccess ? KF_OK : KF_ERR_CUDA;
 }
 

@@ -25,6 +25,8 @@ tensor-op functions below restate that data flow for the CPU tests.
 """
 from __future__ import annotations
 
+import ctypes
+import os
 from dataclasses import dataclass
 from typing import Callable, Optional
 
@@ -97,6 +99,59 @@ def combine(back: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
     return acc.to(torch.bfloat16)
 
 
+class PeerExchange:
+    """This rank's symmetric buffer for the peer-to-peer exchange (``kf_ep_*_p2p``).
+
+    One allocation per rank with the same layout, mapped into every peer by
+    ``torch.distributed``'s symmetric memory (plain NVLink loads and stores; no
+    multicast object is requested).  Layout: barrier flags int32 ``[world]`` |
+    count matrix int32 ``[world, world]`` + status int32 | receive rows
+    ``[T * world, 7456]`` u8 | return rows bf16 ``[max send rows, 7168]``.  The
+    flags and counts are zeroed and all ranks synchronise once (on the host)
+    before the first barrier.
+    """
+
+    def __init__(self, num_tokens: int, world: int, rank: int, group, device: torch.device):
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+        import torch.distributed._symmetric_memory as symm
+        from . import binding as B
+        lib = B.library()
+        self.T, self.world, self.rank, self.device = int(num_tokens), int(world), int(rank), device
+        al = lambda n: (n + 255) // 256 * 256
+        self.max_send = int(lib.kf_ep_max_send_rows(self.T, world))
+        self.off_flags = 0
+        self.off_meta = al(world * 4)
+        self.off_recv = self.off_meta + al((world * world + 1) * 4)
+        self.off_back = self.off_recv + al(self.T * world * ROW_BYTES)
+        total = self.off_back + al(max(self.max_send, 1) * H * 2)
+        self.buf = symm.empty(total, dtype=torch.uint8, device=device)
+        self.buf[:self.off_recv].zero_()
+        torch.cuda.synchronize(device)
+        pg = group if group is not None else dist.group.WORLD
+        self.handle = symm.rendezvous(self.buf, pg.group_name)
+        dist.barrier(group=group)
+        ptrs = [int(x) for x in self.handle.buffer_ptrs]
+        dev_ptrs = lambda off: torch.tensor([p_ + off for p_ in ptrs], dtype=torch.int64, device=device)
+        self.peer_flags = dev_ptrs(self.off_flags)
+        self.peer_counts = dev_ptrs(self.off_meta)
+        self.peer_recv = dev_ptrs(self.off_recv)
+        self.peer_back = dev_ptrs(self.off_back)
+        self.flags = self.buf[self.off_flags:self.off_flags + world * 4].view(torch.int32)
+        self.meta = self.buf[self.off_meta:self.off_meta + (world * world + 1) * 4].view(torch.int32)
+        self.counts = self.meta[:world * world]
+        self.status = self.meta[world * world:]
+        self.recv = self.buf[self.off_recv:self.off_recv + self.T * world * ROW_BYTES].view(self.T * world, ROW_BYTES)
+        self.back = self.buf[self.off_back:self.off_back + self.max_send * H * 2].view(torch.bfloat16).view(-1, H)
+        self.epoch = 0
+
+    def barrier(self, stream) -> None:
+        from . import binding as B
+        self.epoch += 1
+        rc = B.library().kf_ep_barrier(self.peer_flags.data_ptr(), self.flags.data_ptr(), self.rank, self.world,
+                                       self.epoch, self.status.data_ptr(), stream)
+        B._check(rc, "kf_ep_barrier")
+
+
 def _exchange_counts(send_counts: torch.Tensor, group) -> torch.Tensor:
     recv = torch.empty_like(send_counts)
     dist.all_to_all_single(recv, send_counts, group=group)
@@ -130,12 +185,17 @@ class ExpertParallelMoE:
             route_fn = route_fn or binding.route
         self.experts_fn = experts_fn
         self.route_fn = route_fn
-        # "cuda": dispatch / combine / receive-side unpacking in the library's kernels
-        # (the product path); "torch": the tensor-op restatement above, used by the
-        # CPU multi-process tests to check the data flow on gloo ranks
-        if plumbing not in ("cuda", "torch"):
-            raise ValueError("plumbing must be 'cuda' or 'torch'")
+        # "p2p": dispatch rows and returned partials stored straight into the peers'
+        # symmetric buffers by the library's kernels (kf_ep_*_p2p), bounded device
+        # barriers in place of the two NCCL all-to-alls; "cuda": the same kernels
+        # around NCCL all_to_all_single; "torch": the tensor-op restatement above,
+        # used by the CPU multi-process tests to check the data flow on gloo ranks
+        if plumbing not in ("p2p", "cuda", "torch"):
+            raise ValueError("plumbing must be 'p2p', 'cuda' or 'torch'")
+        if plumbing == "p2p" and combine_dtype != torch.bfloat16:
+            raise ValueError("the peer-to-peer exchange returns bf16 partials")
         self.plumbing = plumbing
+        self._peer = None
 
     def local_pairs(self) -> int:
         """(row, local expert) pairs this rank's expert kernels processed in the last forward (synchronises)."""
@@ -146,6 +206,9 @@ class ExpertParallelMoE:
         return int(((ids >= 0) & (loc >= 0) & (loc < self.num_local)).sum().item())
 
     def forward(self, routing_logits, routing_bias, hidden_states, hidden_states_scale, routed_scaling_factor):
+        if self.plumbing == "p2p":
+            return self._forward_p2p(routing_logits, routing_bias, hidden_states, hidden_states_scale,
+                                     routed_scaling_factor)
         if self.plumbing == "cuda":
             return self._forward_cuda(routing_logits, routing_bias, hidden_states, hidden_states_scale,
                                       routed_scaling_factor)
@@ -169,6 +232,46 @@ class ExpertParallelMoE:
         back = torch.empty((S, H), dtype=part.dtype, device=part.device)
         dist.all_to_all_single(back, part, output_split_sizes=s_split, input_split_sizes=r_split, group=self.group)
         return B.ep_combine(back, pos, self.world)
+
+    def _forward_p2p(self, routing_logits, routing_bias, hidden_states, hidden_states_scale, routed_scaling_factor):
+        from . import binding as B
+        lib = B.library()
+        dev = hidden_states.device
+        T = int(hidden_states.shape[0])
+        if self._peer is None or self._peer.T != T:
+            self._peer = PeerExchange(T, self.world, self.rank, self.group, dev)
+        pe = self._peer
+        world, rank = self.world, self.rank
+        idx, w = self.route_fn(routing_logits, routing_bias, routed_scaling_factor)
+        hid = hidden_states.contiguous()
+        hs = hidden_states_scale.contiguous()
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        need = int(lib.kf_ep_workspace_bytes(T, world))
+        ws = B._ep_workspace(dev, need)
+        pos = torch.empty((T, world), dtype=torch.int32, device=dev)
+        sz = ctypes.c_size_t(ws.numel())
+        B._check(lib.kf_ep_plan_p2p(B._ptr(idx), T, world, rank, pe.peer_counts.data_ptr(), B._ptr(ws), sz, stream),
+                 "kf_ep_plan_p2p")
+        pe.barrier(stream)                      # every rank's count row has landed here
+        B._check(lib.kf_ep_pack_p2p(B._ptr(idx), B._ptr(w), B._ptr(hid), B._ptr(hs), T, world, rank,
+                                    pe.counts.data_ptr(), pe.peer_recv.data_ptr(), T * world, B._ptr(pos),
+                                    pe.status.data_ptr(), B._ptr(ws), sz, stream), "kf_ep_pack_p2p")
+        pe.barrier(stream)                      # every row sent to this rank has landed
+        meta = pe.meta.cpu()                    # the step's one host synchronisation
+        if int(meta[world * world]) != 0:
+            raise RuntimeError(f"peer exchange: device status {int(meta[world * world]):#x} "
+                               "(a rank did not reach a barrier)")
+        counts = meta[:world * world].view(world, world)
+        R = int(counts[:, rank].sum())
+        S = int(counts[rank, :].sum())
+        recv = pe.recv[:R]
+        self._last_ids = recv[:, H + HB * 4:H + HB * 4 + TOP_K * 4].contiguous().view(torch.int32)
+        part = B.experts_packed(recv, self.w.gemm1_weights, self.w.gemm1_weights_scale, self.w.gemm2_weights,
+                                self.w.gemm2_weights_scale, self.offset, out_dtype=torch.bfloat16)
+        B._check(lib.kf_ep_return_p2p(B._ptr(part), R, world, rank, pe.counts.data_ptr(), pe.peer_back.data_ptr(),
+                                      stream), "kf_ep_return_p2p")
+        pe.barrier(stream)                      # every partial of this rank's rows is back
+        return B.ep_combine(pe.back[:S], pos, world)
 
     def _forward_torch(self, routing_logits, routing_bias, hidden_states, hidden_states_scale,
                        routed_scaling_factor):

@@ -44,6 +44,18 @@ def worker(rank, world, port, T, result_dir):
         res["ep_vs_ref"] = O.check_tolerance(out, ref.to(torch.bfloat16))
         res["single_vs_ref"] = O.check_tolerance(single, ref.to(torch.bfloat16))
         res["ep_vs_single_maxdiff"] = float((out.float() - single.float()).abs().max())
+        # the peer-to-peer exchange against the NCCL one (same kernels and combine order: bit-identical),
+        # over two steps in a row (the barrier epochs advance and the buffers are reused)
+        nccl = ep.ExpertParallelMoE(shard, rank * E, E, plumbing="cuda")
+        p2p = ep.ExpertParallelMoE(shard, rank * E, E, plumbing="p2p")
+        args = (ti.routing_logits, ti.routing_bias, ti.hidden_states, ti.hidden_states_scale, 2.5)
+        o_nccl = nccl.forward(*args)
+        o_p2p = [p2p.forward(*args) for _ in range(2)]
+        torch.cuda.synchronize(dev)
+        res["p2p_equal_nccl"] = [bool(torch.equal(o, o_nccl)) for o in o_p2p]
+        res["p2p_vs_ref"] = O.check_tolerance(o_p2p[1], ref.to(torch.bfloat16))
+        res["p2p_pairs"] = p2p.local_pairs()
+        res["nccl_pairs"] = nccl.local_pairs()
         dist.barrier()
         dist.destroy_process_group()
     except Exception as exc:

@@ -1,4 +1,4 @@
-"""Expert-parallel layer on 2 GPUs (NCCL) vs the single-GPU layer and the fp32 reference."""
+"""Expert-parallel layer on 2 GPUs (NCCL and the peer-to-peer exchange) vs the single-GPU layer and the fp32 reference."""
 import multiprocessing as mp
 import os
 import socket
@@ -38,3 +38,6 @@ def test_ep_two_gpus(tmp_path):
         assert res["status"] == 0
         assert res["ep_vs_ref"]["ok"], res
         assert res["single_vs_ref"]["ok"], res
+        assert res["p2p_equal_nccl"] == [True, True], res
+        assert res["p2p_vs_ref"]["ok"], res
+        assert res["p2p_pairs"] == res["nccl_pairs"], res
