@@ -16,12 +16,14 @@ the CUDA routing kernel, then:
    output is the sum of its partials in ascending source-rank order (fixed
    order, no atomics), rounded to bf16 once.
 
-The collectives are ``torch.distributed`` all-to-all over NCCL (NVLink /
-NVSwitch); the split sizes are exchanged first (one small all-to-all), which
-is the one host synchronisation of a step.  Dispatch (plan + packing), the
-receive side and the combine run in the library's CUDA kernels
-(``kf_ep_dispatch``, ``kf_moe_experts_packed``, ``kf_ep_combine``); the
-tensor-op functions below restate that data flow for the CPU tests.
+By default the rows and the partials move by stores into the ranks' symmetric
+buffers (``PeerExchange``): the pack kernel writes each row straight into its
+destination's receive area and a return kernel writes each partial back into
+its source's return area, with the library's bounded barrier between the
+phases; reading the count matrix is the one host synchronisation of a step.
+With ``plumbing="cuda"`` the same kernels run around ``torch.distributed``
+all-to-alls over NCCL (split sizes first, then rows).  The tensor-op functions
+below restate the data flow for the CPU tests.
 """
 from __future__ import annotations
 
@@ -169,7 +171,7 @@ class ExpertParallelMoE:
     def __init__(self, weights, local_expert_offset: int, num_local: int, group=None,
                  combine_dtype: torch.dtype = torch.bfloat16,
                  experts_fn: Optional[Callable] = None, route_fn: Optional[Callable] = None,
-                 plumbing: str = "cuda"):
+                 plumbing: str = "p2p"):
         self.w = weights
         self.offset = int(local_expert_offset)
         self.num_local = int(num_local)

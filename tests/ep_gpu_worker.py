@@ -29,7 +29,7 @@ def worker(rank, world, port, T, result_dir):
         E = 256 // world
         ti = S.token_inputs(T, seed=60 + rank, device=dev)
         shard = S.expert_bank(E, rank * E, seed=3, device=dev)
-        layer = ep.ExpertParallelMoE(shard, rank * E, E, combine_dtype=torch.float32)
+        layer = ep.ExpertParallelMoE(shard, rank * E, E, combine_dtype=torch.float32, plumbing="cuda")
         out = layer.forward(ti.routing_logits, ti.routing_bias, ti.hidden_states, ti.hidden_states_scale, 2.5)
         torch.cuda.synchronize(dev)
         res["status"] = B.read_status(dev)
