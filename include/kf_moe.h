@@ -186,6 +186,20 @@ int kf_ep_dispatch(const int32_t* topk_idx, const float* topk_weight, const void
  * reference has no multi-GPU path (the layer's data contract carries
  * local_expert_offset, kernel.py:1826).
  */
+/*
+ * kf_moe_experts_packed for the peer exchange, with the return fused into its
+ * last kernel: instead of writing the bf16 partials locally (for
+ * kf_ep_return_p2p to send), the reduce stores each received row's partial
+ * straight into its source rank's return buffer (peer_back), at the row's
+ * position in the source's send order.  Call it between the second and third
+ * kf_ep_barrier of a step.
+ */
+int kf_moe_experts_packed_p2p(const void* rows, const void* gemm1_weights, const float* gemm1_weights_scale,
+                              const void* gemm2_weights, const float* gemm2_weights_scale, int32_t num_rows,
+                              int32_t num_local_experts, int32_t local_expert_offset, const int32_t* counts,
+                              int32_t rank, int32_t world, void* const* peer_back, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
 int kf_ep_plan_p2p(const int32_t* topk_idx, int32_t num_tokens, int32_t world, int32_t rank,
                    int32_t* const* peer_counts, void* workspace, size_t workspace_bytes, void* stream);
 int kf_ep_pack_p2p(const int32_t* topk_idx, const float* topk_weight, const void* hidden_states,

@@ -74,6 +74,8 @@ def _load():
         lib.kf_ep_pack_p2p.argtypes = [vp, vp, vp, vp, i32, i32, i32, vp, vp, i32, vp, vp, vp, sz, vp]
         lib.kf_ep_return_p2p.restype = ctypes.c_int
         lib.kf_ep_return_p2p.argtypes = [vp, i32, i32, i32, vp, vp, vp]
+        lib.kf_moe_experts_packed_p2p.restype = ctypes.c_int
+        lib.kf_moe_experts_packed_p2p.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32, vp, i32, i32, vp, vp, sz, vp]
         lib.kf_ep_barrier.restype = ctypes.c_int
         lib.kf_ep_barrier.argtypes = [vp, vp, i32, i32, i32, vp, vp]
         lib.kf_quantize_hidden.restype = ctypes.c_int
@@ -287,6 +289,30 @@ def experts_packed(rows, gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm
                                        ctypes.c_void_p(stream.cuda_stream))
     _check(rc, "kf_moe_experts_packed")
     return out
+
+
+def experts_packed_p2p(rows, gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
+                       local_expert_offset, counts, rank: int, world: int, peer_back) -> None:
+    """``experts_packed`` whose reduce stores each row's bf16 partial into its source rank's return buffer.
+
+    ``counts``: this rank's int32 ``[world * world]`` count matrix; ``peer_back``:
+    int64 device tensor of the ``world`` ranks' return-buffer addresses.
+    """
+    device = rows.device
+    R = int(rows.shape[0])
+    if rows.dtype != torch.uint8 or rows.dim() != 2 or rows.shape[1] != PACKED_ROW_BYTES:
+        raise ValueError("rows must be uint8 [R, 7456]")
+    if R == 0:
+        return
+    rows = rows.contiguous()
+    E, w13, w13s, w2, w2s = _weights(gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, device)
+    stream = torch.cuda.current_stream(device)
+    ws = workspace(R, E, device, stream)
+    rc = _load().kf_moe_experts_packed_p2p(_ptr(rows), _ptr(w13), _ptr(w13s), _ptr(w2), _ptr(w2s), R, E,
+                                           _scalar_int(local_expert_offset), _ptr(counts), int(rank), int(world),
+                                           _ptr(peer_back), _ptr(ws), ctypes.c_size_t(ws.numel()),
+                                           ctypes.c_void_p(stream.cuda_stream))
+    _check(rc, "kf_moe_experts_packed_p2p")
 
 
 _ep_ws: dict = {}

@@ -110,7 +110,16 @@ cudaError_t launch_front_small(const float* logits, const void* bias, float rsf,
 cudaError_t launch_gather_rows(const Meta* meta, const int32_t* tile_rows, const int32_t* slot_token,
                                const RowLayout& in, int p_cap, uint8_t* a_rows, float* a_scale, int grid,
                                cudaStream_t s);
-cudaError_t launch_reduce(const int32_t* token_slot, const float* y, int T, void* out, int out_fp32,
+// Expert-parallel receive side over peer memory: the reduce stores each received
+// row's bf16 result straight into its source rank's return buffer (row = the
+// row's position in the source's send order) instead of into a local output.
+struct PeerOut {
+  void* const* peer_back;  // device array: rank q's return buffer (bf16 rows), or null for a local output
+  const int32_t* counts;   // this rank's [world][world] count matrix
+  int rank, world;
+};
+
+cudaError_t launch_reduce(const int32_t* token_slot, const float* y, int T, void* out, int out_fp32, const PeerOut& po,
                           cudaStream_t s);
 
 // The tile fields hold 128-row tiles for the single-CTA kernels and 256-row pair

@@ -174,7 +174,7 @@ constexpr int kSmallT = 32;
 // GEMMs and the reduce, from chunk masks already in the workspace.
 int run_experts(const Workspace& w, void* ws, const RowLayout& in, const void* w13, const float* w13_scale,
                 const void* w2, const float* w2_scale, int T, int E, int offset, void* out, int out_fp32, int num_sms,
-                int pair_clusters, bool front_done, cudaStream_t s) {
+                int pair_clusters, bool front_done, cudaStream_t s, const PeerOut& po = PeerOut{nullptr, nullptr, 0, 1}) {
   int* status = ws_ptr<int>(ws, w.status);
   Meta* meta = ws_ptr<Meta>(ws, w.meta);
   if (!front_done) {
@@ -286,7 +286,7 @@ int run_experts(const Workspace& w, void* ws, const RowLayout& in, const void* w
 
   {
     ProfScope ps(KF_KERNEL_REDUCE, s);
-    if (launch_reduce(ws_ptr<int32_t>(ws, w.token_slot), ws_ptr<float>(ws, w.y), T, out, out_fp32, s) !=
+    if (launch_reduce(ws_ptr<int32_t>(ws, w.token_slot), ws_ptr<float>(ws, w.y), T, out, out_fp32, po, s) !=
         cudaSuccess)
       return KF_ERR_CUDA;
   }
@@ -451,14 +451,16 @@ namespace {
 // kf_moe_experts and kf_moe_experts_packed.
 int experts_common(const RowLayout& in, const void* gemm1_weights, const float* gemm1_weights_scale,
                    const void* gemm2_weights, const float* gemm2_weights_scale, int32_t T, int32_t E, int32_t offset,
-                   void* output, int32_t output_fp32, void* workspace, size_t workspace_bytes, void* stream) {
+                   void* output, int32_t output_fp32, void* workspace, size_t workspace_bytes, void* stream,
+                   const PeerOut& po = PeerOut{nullptr, nullptr, 0, 1}) {
   int rc = check_common(T, E, offset);
   if (rc != KF_OK) return rc;
   if (T == 0) return KF_OK;
-  if (!gemm1_weights || !gemm1_weights_scale || !gemm2_weights || !gemm2_weights_scale || !output || !workspace)
+  if (!gemm1_weights || !gemm1_weights_scale || !gemm2_weights || !gemm2_weights_scale || (!output && !po.peer_back) ||
+      !workspace)
     return KF_ERR_INVALID_ARGUMENT;
-  if (!aligned16(in.hidden) || !aligned16(gemm1_weights) || !aligned16(gemm2_weights) || !aligned16(output) ||
-      !aligned16(workspace))
+  if (!aligned16(in.hidden) || !aligned16(gemm1_weights) || !aligned16(gemm2_weights) ||
+      (output && !aligned16(output)) || !aligned16(workspace))
     return KF_ERR_INVALID_ARGUMENT;
   const Workspace w = plan_workspace(T, E);
   if (workspace_bytes < w.total) return KF_ERR_WORKSPACE_TOO_SMALL;
@@ -478,7 +480,7 @@ int experts_common(const RowLayout& in, const void* gemm1_weights, const float* 
       return KF_ERR_CUDA;
   }
   return run_experts(w, workspace, in, gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, T, E,
-                     offset, output, output_fp32 ? 1 : 0, sms, pair_clusters, small, s);
+                     offset, output, output_fp32 ? 1 : 0, sms, pair_clusters, small, s, po);
 }
 
 }  // namespace
@@ -507,6 +509,18 @@ int kf_moe_experts_packed(const void* rows, const void* gemm1_weights, const flo
   return experts_common(packed_layout(rows), gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
                         num_rows, num_local_experts, local_expert_offset, output, output_fp32, workspace,
                         workspace_bytes, stream);
+}
+
+int kf_moe_experts_packed_p2p(const void* rows, const void* gemm1_weights, const float* gemm1_weights_scale,
+                              const void* gemm2_weights, const float* gemm2_weights_scale, int32_t num_rows,
+                              int32_t num_local_experts, int32_t local_expert_offset, const int32_t* counts,
+                              int32_t rank, int32_t world, void* const* peer_back, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+  if (num_rows > 0 && (!rows || !counts || !peer_back)) return KF_ERR_INVALID_ARGUMENT;
+  if (world < 1 || world > 64 || rank < 0 || rank >= world) return KF_ERR_INVALID_ARGUMENT;
+  return experts_common(packed_layout(rows), gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
+                        num_rows, num_local_experts, local_expert_offset, nullptr, 0, workspace, workspace_bytes,
+                        stream, PeerOut{peer_back, counts, rank, world});
 }
 
 int kf_moe_profile_begin(void) {

@@ -495,8 +495,24 @@ __global__ void __launch_bounds__(kFrontThreads) front_small_kernel(
 // ascending row order (= ascending local expert, the reference's index_add_ order).
 __global__ void __launch_bounds__(256) unpermute_reduce_kernel(const int32_t* __restrict__ token_slot,
                                                      const float* __restrict__ y, int T, void* __restrict__ out,
-                                                     int out_fp32) {
+                                                     int out_fp32, const PeerOut po) {
   const int t = blockIdx.x;
+  __shared__ __nv_bfloat16* peer_row;
+  if (po.peer_back) {
+    // received row t came from source s (sources in rank order) as its j-th row
+    // for this rank; it returns to row (s's rows for lower ranks) + j of s's buffer
+    if (threadIdx.x == 0) {
+      int s = 0, off = 0;
+      while (s + 1 < po.world && off + po.counts[s * po.world + po.rank] <= t) {
+        off += po.counts[s * po.world + po.rank];
+        ++s;
+      }
+      int so = 0;
+      for (int d = 0; d < po.rank; ++d) so += po.counts[s * po.world + d];
+      peer_row = static_cast<__nv_bfloat16*>(po.peer_back[s]) + (static_cast<size_t>(so) + (t - off)) * kH;
+    }
+    __syncthreads();
+  }
   int sl[8];
   int n = 0;
 #pragma unroll
@@ -535,9 +551,11 @@ __global__ void __launch_bounds__(256) unpermute_reduce_kernel(const int32_t* __
       uint2 packed;
       packed.x = *reinterpret_cast<uint32_t*>(&lo);
       packed.y = *reinterpret_cast<uint32_t*>(&hi);
-      reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(out) + static_cast<size_t>(t) * kH)[c] = packed;
+      __nv_bfloat16* row = po.peer_back ? peer_row : static_cast<__nv_bfloat16*>(out) + static_cast<size_t>(t) * kH;
+      reinterpret_cast<uint2*>(row)[c] = packed;
     }
   }
+  if (po.peer_back) __threadfence_system();
 }
 
 }  // namespace
@@ -602,9 +620,9 @@ cudaError_t launch_gather_rows(const Meta* meta, const int32_t* tile_rows, const
   return cudaGetLastError();
 }
 
-cudaError_t launch_reduce(const int32_t* token_slot, const float* y, int T, void* out, int out_fp32,
+cudaError_t launch_reduce(const int32_t* token_slot, const float* y, int T, void* out, int out_fp32, const PeerOut& po,
                           cudaStream_t s) {
-  unpermute_reduce_kernel<<<T, 256, 0, s>>>(token_slot, y, T, out, out_fp32);
+  unpermute_reduce_kernel<<<T, 256, 0, s>>>(token_slot, y, T, out, out_fp32, po);
   return cudaGetLastError();
 }
 

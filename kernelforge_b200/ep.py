@@ -18,9 +18,9 @@ the CUDA routing kernel, then:
 
 By default the rows and the partials move by stores into the ranks' symmetric
 buffers (``PeerExchange``): the pack kernel writes each row straight into its
-destination's receive area and a return kernel writes each partial back into
-its source's return area, with the library's bounded barrier between the
-phases; reading the count matrix is the one host synchronisation of a step.
+destination's receive area and the expert stage's reduce kernel writes each
+partial back into its source's return area, with the library's bounded barrier
+between the phases; reading the count matrix is the one host synchronisation of a step.
 With ``plumbing="cuda"`` the same kernels run around ``torch.distributed``
 all-to-alls over NCCL (split sizes first, then rows).  The tensor-op functions
 below restate the data flow for the CPU tests.
@@ -268,10 +268,10 @@ class ExpertParallelMoE:
         S = int(counts[rank, :].sum())
         recv = pe.recv[:R]
         self._last_ids = recv[:, H + HB * 4:H + HB * 4 + TOP_K * 4].contiguous().view(torch.int32)
-        part = B.experts_packed(recv, self.w.gemm1_weights, self.w.gemm1_weights_scale, self.w.gemm2_weights,
-                                self.w.gemm2_weights_scale, self.offset, out_dtype=torch.bfloat16)
-        B._check(lib.kf_ep_return_p2p(B._ptr(part), R, world, rank, pe.counts.data_ptr(), pe.peer_back.data_ptr(),
-                                      stream), "kf_ep_return_p2p")
+        # the experts' last kernel (the reduce) stores each row's partial straight into
+        # its source's return buffer
+        B.experts_packed_p2p(recv, self.w.gemm1_weights, self.w.gemm1_weights_scale, self.w.gemm2_weights,
+                             self.w.gemm2_weights_scale, self.offset, pe.counts, rank, world, pe.peer_back)
         pe.barrier(stream)                      # every partial of this rank's rows is back
         return B.ep_combine(pe.back[:S], pos, world)
 
