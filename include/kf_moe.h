@@ -175,10 +175,10 @@ int kf_ep_dispatch(const int32_t* topk_idx, const float* topk_weight, const void
  *                     send order
  *   kf_ep_barrier     all partials have landed; kf_ep_combine(return buffer, pos)
  *
- * All ranks pass the same num_tokens; each receive buffer holds recv_capacity
- * = num_tokens * world rows (a row beyond it is dropped and sets
- * KF_STATUS_SLOT_OVERFLOW in *status).  counts is this rank's own (complete)
- * count matrix.  The barrier stores `epoch`
+ * Every rank's receive area holds recv_capacity rows (the same on all ranks; a
+ * row beyond it is dropped and sets KF_STATUS_SLOT_OVERFLOW in *status), which
+ * the caller sizes from the complete count matrix available after the first
+ * barrier.  counts is this rank's own (complete) count matrix.  The barrier stores `epoch`
  * (one more than the previous barrier's) into slot `rank` of every rank's int32
  * flag array (peer_flags; zeroed before the first barrier) and waits, bounded,
  * until its own flags (my_flags) all reach it; a rank that does not arrive sets

@@ -108,24 +108,22 @@ class PeerExchange:
     ``torch.distributed``'s symmetric memory (plain NVLink loads and stores; no
     multicast object is requested).  Layout: barrier flags int32 ``[world]`` |
     count matrix int32 ``[world, world]`` + status int32 | receive rows
-    ``[T * world, 7456]`` u8 | return rows bf16 ``[max send rows, 7168]``.  The
-    flags and counts are zeroed and all ranks synchronise once (on the host)
-    before the first barrier.
+    ``[recv_cap, 7456]`` u8 | return rows bf16 ``[send_cap, 7168]``.  The
+    capacities are the same on every rank.  The flags and counts are zeroed and
+    all ranks synchronise once (on the host) before the first barrier.
     """
 
-    def __init__(self, num_tokens: int, world: int, rank: int, group, device: torch.device):
+    def __init__(self, recv_cap: int, send_cap: int, world: int, rank: int, group, device: torch.device):
         os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
         import torch.distributed._symmetric_memory as symm
-        from . import binding as B
-        lib = B.library()
-        self.T, self.world, self.rank, self.device = int(num_tokens), int(world), int(rank), device
+        self.recv_cap, self.send_cap = int(recv_cap), int(send_cap)
+        self.world, self.rank, self.device = int(world), int(rank), device
         al = lambda n: (n + 255) // 256 * 256
-        self.max_send = int(lib.kf_ep_max_send_rows(self.T, world))
         self.off_flags = 0
         self.off_meta = al(world * 4)
         self.off_recv = self.off_meta + al((world * world + 1) * 4)
-        self.off_back = self.off_recv + al(self.T * world * ROW_BYTES)
-        total = self.off_back + al(max(self.max_send, 1) * H * 2)
+        self.off_back = self.off_recv + al(self.recv_cap * ROW_BYTES)
+        total = self.off_back + al(max(self.send_cap, 1) * H * 2)
         self.buf = symm.empty(total, dtype=torch.uint8, device=device)
         self.buf[:self.off_recv].zero_()
         torch.cuda.synchronize(device)
@@ -142,8 +140,8 @@ class PeerExchange:
         self.meta = self.buf[self.off_meta:self.off_meta + (world * world + 1) * 4].view(torch.int32)
         self.counts = self.meta[:world * world]
         self.status = self.meta[world * world:]
-        self.recv = self.buf[self.off_recv:self.off_recv + self.T * world * ROW_BYTES].view(self.T * world, ROW_BYTES)
-        self.back = self.buf[self.off_back:self.off_back + self.max_send * H * 2].view(torch.bfloat16).view(-1, H)
+        self.recv = self.buf[self.off_recv:self.off_recv + self.recv_cap * ROW_BYTES].view(self.recv_cap, ROW_BYTES)
+        self.back = self.buf[self.off_back:self.off_back + self.send_cap * H * 2].view(torch.bfloat16).view(-1, H)
         self.epoch = 0
 
     def barrier(self, stream) -> None:
@@ -240,32 +238,46 @@ class ExpertParallelMoE:
         lib = B.library()
         dev = hidden_states.device
         T = int(hidden_states.shape[0])
-        if self._peer is None or self._peer.T != T:
-            self._peer = PeerExchange(T, self.world, self.rank, self.group, dev)
-        pe = self._peer
         world, rank = self.world, self.rank
+        if self._peer is None:
+            # capacities for the largest rank's token count (agreed once, on the device)
+            t = torch.tensor([T], dtype=torch.int64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+            t_max = int(t.item())
+            self._peer = PeerExchange(t_max * world, int(lib.kf_ep_max_send_rows(t_max, world)), world, rank,
+                                      self.group, dev)
         idx, w = self.route_fn(routing_logits, routing_bias, routed_scaling_factor)
         hid = hidden_states.contiguous()
         hs = hidden_states_scale.contiguous()
         stream = torch.cuda.current_stream(dev).cuda_stream
-        need = int(lib.kf_ep_workspace_bytes(T, world))
-        ws = B._ep_workspace(dev, need)
-        pos = torch.empty((T, world), dtype=torch.int32, device=dev)
+        ws = B._ep_workspace(dev, int(lib.kf_ep_workspace_bytes(T, world)))
         sz = ctypes.c_size_t(ws.numel())
-        B._check(lib.kf_ep_plan_p2p(B._ptr(idx), T, world, rank, pe.peer_counts.data_ptr(), B._ptr(ws), sz, stream),
-                 "kf_ep_plan_p2p")
-        pe.barrier(stream)                      # every rank's count row has landed here
-        B._check(lib.kf_ep_pack_p2p(B._ptr(idx), B._ptr(w), B._ptr(hid), B._ptr(hs), T, world, rank,
-                                    pe.counts.data_ptr(), pe.peer_recv.data_ptr(), T * world, B._ptr(pos),
-                                    pe.status.data_ptr(), B._ptr(ws), sz, stream), "kf_ep_pack_p2p")
-        pe.barrier(stream)                      # every row sent to this rank has landed
-        meta = pe.meta.cpu()                    # the step's one host synchronisation
-        if int(meta[world * world]) != 0:
-            raise RuntimeError(f"peer exchange: device status {int(meta[world * world]):#x} "
-                               "(a rank did not reach a barrier)")
-        counts = meta[:world * world].view(world, world)
+
+        def plan(pe):
+            B._check(lib.kf_ep_plan_p2p(B._ptr(idx), T, world, rank, pe.peer_counts.data_ptr(), B._ptr(ws), sz,
+                                        stream), "kf_ep_plan_p2p")
+            pe.barrier(stream)                  # every rank's count row has landed here
+            meta = pe.meta.cpu()                # the step's one host synchronisation
+            if int(meta[world * world]) != 0:
+                raise RuntimeError(f"peer exchange: device status {int(meta[world * world]):#x} "
+                                   "(a rank did not reach a barrier, or a receive area overflowed)")
+            return meta[:world * world].view(world, world)
+
+        counts = plan(self._peer)
+        # every rank holds the same count matrix, so all of them take this branch together
+        need_recv, need_send = int(counts.sum(0).max()), int(counts.sum(1).max())
+        if need_recv > self._peer.recv_cap or need_send > self._peer.send_cap:
+            self._peer = PeerExchange(max(need_recv, self._peer.recv_cap), max(need_send, self._peer.send_cap),
+                                      world, rank, self.group, dev)
+            counts = plan(self._peer)
+        pe = self._peer
         R = int(counts[:, rank].sum())
         S = int(counts[rank, :].sum())
+        pos = torch.empty((T, world), dtype=torch.int32, device=dev)
+        B._check(lib.kf_ep_pack_p2p(B._ptr(idx), B._ptr(w), B._ptr(hid), B._ptr(hs), T, world, rank,
+                                    pe.counts.data_ptr(), pe.peer_recv.data_ptr(), pe.recv_cap, B._ptr(pos),
+                                    pe.status.data_ptr(), B._ptr(ws), sz, stream), "kf_ep_pack_p2p")
+        pe.barrier(stream)                      # every row sent to this rank has landed
         recv = pe.recv[:R]
         self._last_ids = recv[:, H + HB * 4:H + HB * 4 + TOP_K * 4].contiguous().view(torch.int32)
         # the experts' last kernel (the reduce) stores each row's partial straight into

@@ -56,6 +56,22 @@ def worker(rank, world, port, T, result_dir):
         res["p2p_vs_ref"] = O.check_tolerance(o_p2p[1], ref.to(torch.bfloat16))
         res["p2p_pairs"] = p2p.local_pairs()
         res["nccl_pairs"] = nccl.local_pairs()
+        # uneven token counts (one rank empty in the second step): the receive and return areas are
+        # sized from the count matrix every rank holds, and grow together when a step needs more
+        uneven = ep.ExpertParallelMoE(shard, rank * E, E, plumbing="p2p")
+        res["uneven"] = []
+        for step, Ts in enumerate(([64, 32], [700, 0])):
+            tu = S.token_inputs(Ts[rank], seed=90 + 10 * step + rank, device=dev)
+            ou = uneven.forward(tu.routing_logits, tu.routing_bias, tu.hidden_states, tu.hidden_states_scale, 2.5)
+            torch.cuda.synchronize(dev)
+            if Ts[rank] == 0:
+                res["uneven"].append({"ok": tuple(ou.shape) == (0, 7168)})
+                continue
+            iu, wu = B.route(tu.routing_logits, tu.routing_bias, 2.5)
+            ru = O.moe_experts(iu, wu, tu.hidden_states, tu.hidden_states_scale, full.gemm1_weights,
+                               full.gemm1_weights_scale, full.gemm2_weights, full.gemm2_weights_scale, 0)
+            res["uneven"].append(O.check_tolerance(ou, ru.to(torch.bfloat16)))
+        res["uneven_caps"] = (uneven._peer.recv_cap, uneven._peer.send_cap)
         dist.barrier()
         dist.destroy_process_group()
     except Exception as exc:

@@ -41,3 +41,4 @@ def test_ep_two_gpus(tmp_path):
         assert res["p2p_equal_nccl"] == [True, True], res
         assert res["p2p_vs_ref"]["ok"], res
         assert res["p2p_pairs"] == res["nccl_pairs"], res
+        assert all(u["ok"] for u in res["uneven"]), res["uneven"]
