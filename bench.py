@@ -40,6 +40,10 @@ sys.path.insert(0, ROOT)
 H, I, E_GLOBAL = 7168, 2048, 256
 FLOP_PER_PAIR = 2 * (2 * I * H + H * I)            # 88,080,384
 GEMM1_FLOP_PER_PAIR = 2 * 2 * I * H                # 58,720,256
+W13_BYTES_PER_EXPERT = 2 * I * H                   # 29,360,128 (e4m3)
+W2_BYTES_PER_EXPERT = H * I                        # 14,680,064
+W13_SCALE_BYTES = (2 * I // 128) * (H // 128) * 4
+W2_SCALE_BYTES = (H // 128) * (I // 128) * 4
 METRIC = "MoE layer tokens/s (FP8 block-scale DeepSeek-V3 layer, T=8192 tokens per GPU, 256 experts EP-sharded)"
 
 
@@ -53,6 +57,8 @@ def parse():
     p.add_argument("--tokens", type=int, default=None)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--graph", action="store_true", help="replay the layer as a CUDA graph (1 GPU)")
+    p.add_argument("--zipf", action="store_true",
+                   help="config 4: routing bias skewing expert popularity to Zipf(1.2) over a seeded permutation")
     p.add_argument("--ep-exchange", default="p2p", choices=["p2p", "nccl"],
                    help="N > 1: peer-to-peer stores into symmetric buffers, or NCCL all-to-all")
     return p.parse_args()
@@ -216,7 +222,10 @@ def main():
     offset = rank * E if args.workload == "ep" else 0
     peaks = load_peaks()
 
-    ti = S.token_inputs(T, seed=17 + rank, device=dev)
+    bias = S.zipf_bias(seed=0).to(dev) if args.zipf else None
+    ti = S.token_inputs(T, seed=17 + rank, device=dev, routing_bias=bias)
+    if args.zipf:
+        name += "_zipf1.2"
     wb = S.expert_bank(E, offset, seed=0, device=dev)
     torch.cuda.synchronize(dev)
 
@@ -236,9 +245,11 @@ def main():
         graphed = GraphedMoE(wb, offset, 2.5, T).capture()
         step = graphed
 
-    # local (token, expert) pairs of this rank's GEMMs (for the FLOP count)
+    # local (token, expert) pairs of this rank's GEMMs (for the FLOP count) and the local
+    # experts that receive at least one pair (whose weights a step must read)
     idx, _ = B.route(ti.routing_logits, ti.routing_bias, 2.5)
     pairs = int(((idx >= offset) & (idx < offset + E)).sum().item()) if world == 1 else None
+    active = int(torch.unique(idx[(idx >= offset) & (idx < offset + E)]).numel()) if world == 1 else None
 
     def barrier():
         if world > 1:
@@ -361,7 +372,16 @@ def main():
     g2_ms, g2_n = prof["gemm2_weighted"]
     total_launches = sum(n for _, n in prof.values())   # launches in K profiled steps = launches in K timed steps
     roofline = None
-    if g1_n and pairs is not None:
+    if g1_n and pairs is not None and args.workload == "decode":
+        # decode is weight-streaming bound: GEMM1 reads the W13 tiles (and scales) of every active expert
+        g1_avg = g1_ms / g1_n
+        g1_bytes = active * (W13_BYTES_PER_EXPERT + W13_SCALE_BYTES) + pairs * (H + H // 128 * 4)
+        achieved = g1_bytes / (g1_avg / 1e3) / 1e9
+        roofline = {"bound": "hbm", "kernel": "gemm1_swiglu", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                    "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                    "peak_note": f"{peaks['source']} HBM copy bandwidth", "avg_launch_ms": g1_avg,
+                    "active_experts": active}
+    elif g1_n and pairs is not None:
         g1_avg = g1_ms / g1_n
         achieved = GEMM1_FLOP_PER_PAIR * pairs / (g1_avg / 1e3) / 1e12
         peak = 2.0 * peaks["bf16_sustained"]
@@ -398,6 +418,9 @@ def main():
                        "pairs_rank0": pairs, "cuda_graph": bool(args.graph and world == 1)},
             "p50_step_ms": step_ms[len(step_ms) // 2], "p90_step_ms": step_ms[int(len(step_ms) * 0.9)],
             "tflops_per_gpu": (FLOP_PER_PAIR * pairs / (ms_per_step / 1e3) / 1e12) if pairs else None,
+            "layer_hbm_gbs": (active * (W13_BYTES_PER_EXPERT + W2_BYTES_PER_EXPERT + W13_SCALE_BYTES + W2_SCALE_BYTES)
+                              / (ms_per_step / 1e3) / 1e9) if active else None,
+            "active_local_experts": active,
             "roofline": roofline, "kernels": kernels, "gpu_launches": total_launches,
             "e2e": e2e, "cpu_baseline": cpu,
             "clocks": clocks.summary(t_wall0, t_wall1),
