@@ -138,6 +138,8 @@ struct ArmedSlots {
 __global__ void __launch_bounds__(kThreads, 1)
     gemm1_swiglu_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_a32,
                         const __grid_constant__ CUtensorMap tm_w, const Gemm1Args g) {
+  grid_dep_wait();
+  grid_dep_trigger();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sA = smem;
@@ -469,6 +471,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm2_weighted_kernel(const __grid_constant__ CUtensorMap tm_chi, const __grid_constant__ CUtensorMap tm_clo,
                           const __grid_constant__ CUtensorMap tm_chi32, const __grid_constant__ CUtensorMap tm_clo32,
                           const __grid_constant__ CUtensorMap tm_w, const Gemm2Args g) {
+  grid_dep_wait();
+  grid_dep_trigger();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sAhi = smem;
@@ -688,6 +692,8 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(const Meta* __restric
                                                            const float* __restrict__ partial, int ksplit,
                                                            int max_pairs, int p_cap, uint8_t* __restrict__ c_hi,
                                                            uint8_t* __restrict__ c_lo, float* __restrict__ c_scale) {
+  grid_dep_wait();
+  grid_dep_trigger();
   const int lane = threadIdx.x & 31;
   const int warps = blockDim.x >> 5;
   const int nwork = meta->num_tiles * kBlk * kIB;
@@ -727,21 +733,18 @@ cudaError_t gemm_set_attributes() {
 
 cudaError_t launch_gemm1(const CUtensorMap& tm_a, const CUtensorMap& tm_a32, const CUtensorMap& tm_w13,
                          const Gemm1Args& args, int grid, cudaStream_t s) {
-  gemm1_swiglu_kernel<<<grid, kThreads, G1_SMEM, s>>>(tm_a, tm_a32, tm_w13, args);
-  return cudaGetLastError();
+  return launch_chained(gemm1_swiglu_kernel, dim3(grid), dim3(kThreads), G1_SMEM, s, tm_a, tm_a32, tm_w13, args);
 }
 
 cudaError_t launch_swiglu_quant(const Gemm1Args& g, int grid, cudaStream_t s) {
-  swiglu_quant_kernel<<<grid, 256, 0, s>>>(g.meta, g.tile_rows, g.slot_pair, g.partial, g.ksplit, g.max_pairs,
+  return launch_chained(swiglu_quant_kernel, dim3(grid), dim3(256), 0, s, g.meta, g.tile_rows, g.slot_pair, g.partial, g.ksplit, g.max_pairs,
                                            g.p_cap, g.c_hi, g.c_lo, g.c_scale);
-  return cudaGetLastError();
 }
 
 cudaError_t launch_gemm2(const CUtensorMap& tm_chi, const CUtensorMap& tm_clo, const CUtensorMap& tm_chi32,
                          const CUtensorMap& tm_clo32, const CUtensorMap& tm_w2, const Gemm2Args& args, int grid,
                          cudaStream_t s) {
-  gemm2_weighted_kernel<<<grid, kThreads, G2_SMEM, s>>>(tm_chi, tm_clo, tm_chi32, tm_clo32, tm_w2, args);
-  return cudaGetLastError();
+  return launch_chained(gemm2_weighted_kernel, dim3(grid), dim3(kThreads), G2_SMEM, s, tm_chi, tm_clo, tm_chi32, tm_clo32, tm_w2, args);
 }
 
 }  // namespace kf

@@ -5,6 +5,7 @@
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <utility>
 
 #include "kf_moe.h"
 
@@ -86,6 +87,27 @@ inline RowLayout packed_layout(const void* rows) {
   return RowLayout{reinterpret_cast<const int32_t*>(b + kH + kHB * 4),
                    reinterpret_cast<const float*>(b + kH + kHB * 4 + kTopK * 4), kPackedRowBytes / 4, b,
                    kPackedRowBytes, reinterpret_cast<const float*>(b + kH), kPackedRowBytes / 4, 1};
+}
+
+// Programmatic dependent launch for the layer's launch chain (on unless the
+// environment sets KF_MOE_PDL=0): a kernel launched this way may start while its
+// predecessor in the stream is finishing, and must begin with grid_dep_wait().
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_chained(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                           Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // Kernel launchers (return cudaGetLastError()).

@@ -16,6 +16,15 @@
 
 namespace kf {
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("KF_MOE_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+
 namespace {
 
 constexpr size_t kAlign = 256;

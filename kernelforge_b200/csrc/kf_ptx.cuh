@@ -25,6 +25,18 @@ __device__ __forceinline__ void record_error(int* status, int code) {
   if (status) atomicOr(status, code);
 }
 
+// ------------------------------------------------- programmatic dependent launch --
+// Kernels of the layer's launch chain may be launched before their predecessor
+// has finished (cudaLaunchAttributeProgrammaticStreamSerialization).  Every such
+// kernel calls grid_dep_wait() before it touches memory a predecessor writes:
+// it returns once the preceding grid has completed and its writes are visible
+// (immediately when the launch was an ordinary one).  grid_dep_trigger() lets the
+// next kernel in the stream start launching; only kernels whose CTAs are all
+// resident at once (persistent or single-CTA grids) call it, so CTAs of the next
+// kernel that wait in grid_dep_wait() can never keep a CTA of this one off an SM.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_trigger() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 // ---------------------------------------------------------------- mbarrier --
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");

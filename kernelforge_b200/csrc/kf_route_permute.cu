@@ -151,6 +151,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const float* __res
                                                               float rsf, int32_t* __restrict__ topk_idx,
                                                               float* __restrict__ topk_w, int E, int offset,
                                                               uint32_t* __restrict__ chunk_masks) {
+  grid_dep_wait();
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * (kRouteThreads / 32) + (threadIdx.x >> 5);
   if (t >= T) return;
@@ -174,6 +175,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const float* __res
 // Token bitmasks per local expert from externally supplied routing (expert-parallel receive side).
 __global__ void __launch_bounds__(256) masks_from_topk_kernel(const RowLayout in, int T, int E, int offset,
                                                               uint4* __restrict__ chunk_masks, int* status) {
+  grid_dep_wait();
   __shared__ uint32_t masks[kMaxLocalExperts * 4];
   const int chunk = blockIdx.x;
   for (int i = threadIdx.x; i < E * 4; i += blockDim.x) masks[i] = 0u;
@@ -204,6 +206,8 @@ __global__ void __launch_bounds__(kMaxLocalExperts) permute_scan_kernel(
     int32_t* __restrict__ chunk_base, int32_t* __restrict__ tile_expert, int32_t* __restrict__ tile_row0,
     int32_t* __restrict__ tile_rows, int32_t* __restrict__ ptile_expert, int32_t* __restrict__ ptile_row0,
     int32_t* __restrict__ ptile_rows, int nt_cap, int* status) {
+  grid_dep_wait();
+  grid_dep_trigger();
   __shared__ int32_t tiles_scan[kMaxLocalExperts];
   __shared__ int32_t ptiles_scan[kMaxLocalExperts];
   __shared__ int32_t pairs_scan[kMaxLocalExperts];
@@ -292,6 +296,7 @@ __global__ void __launch_bounds__(256) permute_assign_kernel(
     const int32_t* __restrict__ chunk_base, const Meta* __restrict__ meta, int T, int E, int offset, int p_cap,
     int32_t* __restrict__ token_slot, int32_t* __restrict__ slot_token, float* __restrict__ slot_weight,
     int32_t* __restrict__ slot_pair, int* status) {
+  grid_dep_wait();
   __shared__ uint4 masks[kMaxLocalExperts];
   __shared__ int32_t base[kMaxLocalExperts];
   const int chunk = blockIdx.x;
@@ -339,6 +344,7 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const Meta* __restrict
                                                           const RowLayout in, int p_cap,
                                                           uint8_t* __restrict__ a_rows,
                                                           float* __restrict__ a_scale) {
+  grid_dep_wait();
   const int lane = threadIdx.x & 31;
   const int warps = blockDim.x >> 5;
   const int nrows = meta->num_tiles * kBlk;
@@ -371,6 +377,8 @@ __global__ void __launch_bounds__(kFrontThreads) front_small_kernel(
     int32_t* __restrict__ ptile_expert, int32_t* __restrict__ ptile_row0, int32_t* __restrict__ ptile_rows,
     int32_t* __restrict__ token_slot, int32_t* __restrict__ slot_token, float* __restrict__ slot_weight,
     int32_t* __restrict__ slot_pair, uint8_t* __restrict__ a_rows, float* __restrict__ a_scale, int* status) {
+  grid_dep_wait();
+  grid_dep_trigger();
   __shared__ uint32_t masks[kMaxLocalExperts * 4];
   __shared__ int32_t tk[kChunkTokens * kTopK];
   __shared__ float tw[kChunkTokens * kTopK];
@@ -496,6 +504,7 @@ __global__ void __launch_bounds__(kFrontThreads) front_small_kernel(
 __global__ void __launch_bounds__(256) unpermute_reduce_kernel(const int32_t* __restrict__ token_slot,
                                                      const float* __restrict__ y, int T, void* __restrict__ out,
                                                      int out_fp32, const PeerOut po) {
+  grid_dep_wait();
   const int t = blockIdx.x;
   __shared__ __nv_bfloat16* peer_row;
   if (po.peer_back) {
@@ -568,26 +577,23 @@ cudaError_t launch_route(const float* logits, const void* bias, int T, float rsf
     if (e != cudaSuccess) return e;
   }
   const int warps = kRouteThreads / 32;
-  route_kernel<<<(T + warps - 1) / warps, kRouteThreads, 0, s>>>(logits, static_cast<const __nv_bfloat16*>(bias), T,
+  return launch_chained(route_kernel, dim3((T + warps - 1) / warps), dim3(kRouteThreads), 0, s, logits, static_cast<const __nv_bfloat16*>(bias), T,
                                                                  rsf, topk_idx, topk_w, E, offset,
                                                                  reinterpret_cast<uint32_t*>(chunk_masks));
-  return cudaGetLastError();
 }
 
 cudaError_t launch_masks_from_topk(const RowLayout& in, int T, int E, int offset, uint4* chunk_masks, int* status,
                                    cudaStream_t s) {
   const int nchunk = (T + kChunkTokens - 1) / kChunkTokens;
-  masks_from_topk_kernel<<<nchunk, 256, 0, s>>>(in, T, E, offset, chunk_masks, status);
-  return cudaGetLastError();
+  return launch_chained(masks_from_topk_kernel, dim3(nchunk), dim3(256), 0, s, in, T, E, offset, chunk_masks, status);
 }
 
 cudaError_t launch_permute_scan(const uint4* chunk_masks, int nchunk, int E, Meta* meta, int32_t* chunk_base,
                                 int32_t* tile_expert, int32_t* tile_row0, int32_t* tile_rows, int32_t* ptile_expert,
                                 int32_t* ptile_row0, int32_t* ptile_rows, int nt_cap, int* status, cudaStream_t s) {
-  permute_scan_kernel<<<1, kMaxLocalExperts, 0, s>>>(chunk_masks, nchunk, E, meta, chunk_base, tile_expert,
+  return launch_chained(permute_scan_kernel, dim3(1), dim3(kMaxLocalExperts), 0, s, chunk_masks, nchunk, E, meta, chunk_base, tile_expert,
                                                      tile_row0, tile_rows, ptile_expert, ptile_row0, ptile_rows,
                                                      nt_cap, status);
-  return cudaGetLastError();
 }
 
 cudaError_t launch_permute_assign(const RowLayout& in, const uint4* chunk_masks, const int32_t* chunk_base,
@@ -595,9 +601,8 @@ cudaError_t launch_permute_assign(const RowLayout& in, const uint4* chunk_masks,
                                   int32_t* slot_token, float* slot_weight, int32_t* slot_pair, int* status,
                                   cudaStream_t s) {
   const int nchunk = (T + kChunkTokens - 1) / kChunkTokens;
-  permute_assign_kernel<<<nchunk, 256, 0, s>>>(in, chunk_masks, chunk_base, meta, T, E, offset, p_cap, token_slot,
+  return launch_chained(permute_assign_kernel, dim3(nchunk), dim3(256), 0, s, in, chunk_masks, chunk_base, meta, T, E, offset, p_cap, token_slot,
                                                slot_token, slot_weight, slot_pair, status);
-  return cudaGetLastError();
 }
 
 cudaError_t launch_front_small(const float* logits, const void* bias, float rsf, const RowLayout& in, int T, int E,
@@ -605,25 +610,22 @@ cudaError_t launch_front_small(const float* logits, const void* bias, float rsf,
                                int32_t* tile_rows, int32_t* ptile_expert, int32_t* ptile_row0, int32_t* ptile_rows,
                                int32_t* token_slot, int32_t* slot_token, float* slot_weight, int32_t* slot_pair,
                                uint8_t* a_rows, float* a_scale, int* status, cudaStream_t s) {
-  front_small_kernel<<<1, kFrontThreads, 0, s>>>(logits, static_cast<const __nv_bfloat16*>(bias), rsf, in, T, E,
+  return launch_chained(front_small_kernel, dim3(1), dim3(kFrontThreads), 0, s, logits, static_cast<const __nv_bfloat16*>(bias), rsf, in, T, E,
                                                  offset, p_cap, meta,
                                                  tile_expert, tile_row0, tile_rows, ptile_expert, ptile_row0,
                                                  ptile_rows, token_slot, slot_token, slot_weight, slot_pair, a_rows,
                                                  a_scale, status);
-  return cudaGetLastError();
 }
 
 cudaError_t launch_gather_rows(const Meta* meta, const int32_t* tile_rows, const int32_t* slot_token,
                                const RowLayout& in, int p_cap, uint8_t* a_rows, float* a_scale, int grid,
                                cudaStream_t s) {
-  gather_rows_kernel<<<grid, 256, 0, s>>>(meta, tile_rows, slot_token, in, p_cap, a_rows, a_scale);
-  return cudaGetLastError();
+  return launch_chained(gather_rows_kernel, dim3(grid), dim3(256), 0, s, meta, tile_rows, slot_token, in, p_cap, a_rows, a_scale);
 }
 
 cudaError_t launch_reduce(const int32_t* token_slot, const float* y, int T, void* out, int out_fp32, const PeerOut& po,
                           cudaStream_t s) {
-  unpermute_reduce_kernel<<<T, 256, 0, s>>>(token_slot, y, T, out, out_fp32, po);
-  return cudaGetLastError();
+  return launch_chained(unpermute_reduce_kernel, dim3(T), dim3(256), 0, s, token_slot, y, T, out, out_fp32, po);
 }
 
 }  // namespace kf
