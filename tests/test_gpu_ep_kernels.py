@@ -59,3 +59,104 @@ def test_combine_matches_restatement(dtype):
     ref = ep.combine(back, pos.long())
     torch.cuda.synchronize()
     assert torch.equal(out, ref)
+
+
+# ---------------------------------------------------------------- peer exchange --
+# The peer-to-peer kernels with the ranks emulated on one GPU: every "peer"
+# pointer points at another local buffer, and the ranks' kernels run one after
+# the other on one stream (their stream order stands in for the barriers).
+
+
+def _ptrs(ts):
+    return torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64, device="cuda")
+
+
+def _emulated_ranks(world, T):
+    lib = B.library()
+    ranks = []
+    for r in range(world):
+        ti = to_cuda(S.token_inputs(T, seed=200 + r))
+        idx, w = B.route(ti.routing_logits, ti.routing_bias, 2.5)
+        ranks.append({"ti": ti, "idx": idx, "w": w,
+                      "counts": torch.zeros(world * world, dtype=torch.int32, device="cuda"),
+                      "recv": torch.zeros((T * world, ep.ROW_BYTES), dtype=torch.uint8, device="cuda"),
+                      "back": torch.zeros((int(lib.kf_ep_max_send_rows(T, world)), B.H), dtype=torch.bfloat16,
+                                          device="cuda"),
+                      "ws": torch.zeros(max(int(lib.kf_ep_workspace_bytes(T, world)), 256), dtype=torch.uint8,
+                                        device="cuda"),
+                      "pos": torch.empty((T, world), dtype=torch.int32, device="cuda"),
+                      "status": torch.zeros(1, dtype=torch.int32, device="cuda")})
+    stream = torch.cuda.current_stream().cuda_stream
+    peer_counts = _ptrs([x["counts"] for x in ranks])
+    peer_recv = _ptrs([x["recv"] for x in ranks])
+    for r, x in enumerate(ranks):
+        rc = lib.kf_ep_plan_p2p(B._ptr(x["idx"]), T, world, r, peer_counts.data_ptr(), B._ptr(x["ws"]),
+                                x["ws"].numel(), stream)
+        assert rc == 0
+    for r, x in enumerate(ranks):
+        rc = lib.kf_ep_pack_p2p(B._ptr(x["idx"]), B._ptr(x["w"]), B._ptr(x["ti"].hidden_states),
+                                B._ptr(x["ti"].hidden_states_scale), T, world, r, x["counts"].data_ptr(),
+                                peer_recv.data_ptr(), T * world, B._ptr(x["pos"]), x["status"].data_ptr(),
+                                B._ptr(x["ws"]), x["ws"].numel(), stream)
+        assert rc == 0
+    torch.cuda.synchronize()
+    return ranks
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_peer_pack_matches_dispatch(world):
+    """Every rank's receive area = the sources' dispatch rows for it, in source order; counts and pos as dispatch."""
+    T = 300
+    ranks = _emulated_ranks(world, T)
+    sends = [B.ep_dispatch(x["idx"], x["w"], x["ti"].hidden_states, x["ti"].hidden_states_scale, world)
+             for x in ranks]
+    torch.cuda.synchronize()
+    counts = torch.stack([c.cpu() for _, c, _ in sends]).to(torch.int32)        # [source, dest]
+    for r, x in enumerate(ranks):
+        assert torch.equal(x["counts"].cpu().view(world, world), counts)          # every rank holds the full matrix
+        assert torch.equal(x["pos"], sends[r][2])
+        assert int(x["status"].item()) == 0
+    for d, x in enumerate(ranks):
+        parts = []
+        for s in range(world):
+            off = int(counts[s, :d].sum())
+            parts.append(sends[s][0][off:off + int(counts[s, d])])
+        expect = torch.cat(parts)
+        assert torch.equal(x["recv"][:expect.shape[0]], expect)
+
+
+def test_peer_return_fused_into_reduce():
+    """experts_packed_p2p stores each partial at its source's send position: the same rows experts_packed returns."""
+    world, T = 2, 300
+    E = 256 // world
+    ranks = _emulated_ranks(world, T)
+    counts = ranks[0]["counts"].cpu().view(world, world)
+    banks = [gpu_bank(E, d * E, seed=5) for d in range(world)]
+    peer_back = _ptrs([x["back"] for x in ranks])
+    partials = []
+    for d, x in enumerate(ranks):
+        R = int(counts[:, d].sum())
+        rows = x["recv"][:R]
+        wb = banks[d]
+        partials.append(B.experts_packed(rows, wb.gemm1_weights, wb.gemm1_weights_scale, wb.gemm2_weights,
+                                         wb.gemm2_weights_scale, d * E))
+        B.experts_packed_p2p(rows, wb.gemm1_weights, wb.gemm1_weights_scale, wb.gemm2_weights,
+                             wb.gemm2_weights_scale, d * E, x["counts"], d, world, peer_back)
+    torch.cuda.synchronize()
+    for s, x in enumerate(ranks):
+        expect = torch.cat([partials[d][int(counts[:s, d].sum()):int(counts[:s + 1, d].sum())] for d in range(world)])
+        assert torch.equal(x["back"][:expect.shape[0]], expect)
+
+
+def test_peer_barrier_times_out_instead_of_hanging():
+    """A rank that never arrives: the barrier gives up after its bounded wait and reports it (no trap, no hang)."""
+    lib = B.library()
+    flags = [torch.zeros(2, dtype=torch.int32, device="cuda") for _ in range(2)]
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    peer_flags = _ptrs(flags)
+    rc = lib.kf_ep_barrier(peer_flags.data_ptr(), flags[0].data_ptr(), 0, 2, 1, status.data_ptr(),
+                           torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert int(status.item()) & 0x20            # KF_STATUS_TIMEOUT_PEER
+    assert flags[0].tolist() == [1, 0] and flags[1].tolist() == [1, 0]   # its own arrival reached both ranks
