@@ -66,7 +66,11 @@ constexpr int G2_OFF_B = 2 * G2_S * G2_A;
 constexpr int G2_OFF_BAR = G2_OFF_B + G2_S * G2_B;
 constexpr int G2_NBAR = 2 * G2_S + 4;
 constexpr int G2_OFF_MISC = G2_OFF_BAR + G2_NBAR * 8;
-constexpr int G2_SMEM = G2_OFF_MISC + 16 + 1024;
+// Epilogue staging for TMA stores of y: per promotion warp 32 rows x 32 fp32
+// columns (4 KB, 128-byte swizzled as the y tensor map expects), 1024-aligned.
+constexpr int G2_STG_WARP = 32 * 32 * 4;
+constexpr int G2_OFF_STG = (G2_OFF_MISC + 16 + 1023) / 1024 * 1024;
+constexpr int G2_SMEM = G2_OFF_STG + kEpiWarps * G2_STG_WARP + 1024;
 constexpr int kG2NB = kH / 256;  // 28 column blocks of 256
 
 static_assert(G1_SMEM <= 232448, "GEMM1 shared memory");
@@ -419,31 +423,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
-// In-register transpose of an 8x8 block of float4 across the 8 lanes of a lane
-// group (gl = lane & 7): on entry lane i holds v[j] = element (i, j); on exit
-// lane i holds v[j] = element (j, i).  Three butterfly stages; each exchanges
-// half of the registers with the lane gl ^ s.  The whole warp must call it.
-__device__ __forceinline__ void transpose8_f4(float4 (&v)[8], int gl) {
-#pragma unroll
-  for (int s = 4; s >= 1; s >>= 1) {
-    const bool upper = (gl & s) != 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if (j & s) continue;
-      const float4 send = upper ? v[j] : v[j | s];
-      float4 recv;
-      recv.x = __shfl_xor_sync(0xffffffffu, send.x, s);
-      recv.y = __shfl_xor_sync(0xffffffffu, send.y, s);
-      recv.z = __shfl_xor_sync(0xffffffffu, send.z, s);
-      recv.w = __shfl_xor_sync(0xffffffffu, send.w, s);
-      if (upper)
-        v[j] = recv;
-      else
-        v[j | s] = recv;
-    }
-  }
-}
-
 // A GEMM2 work unit as the promotion warps see it (tile entry read one unit ahead).
 struct G2Unit {
   int nb2, e, row0, nrows;
@@ -470,7 +449,8 @@ __device__ __forceinline__ void g2_scales(const Gemm2Args& g, const G2Unit& w, i
 __global__ void __launch_bounds__(kThreads, 1)
     gemm2_weighted_kernel(const __grid_constant__ CUtensorMap tm_chi, const __grid_constant__ CUtensorMap tm_clo,
                           const __grid_constant__ CUtensorMap tm_chi32, const __grid_constant__ CUtensorMap tm_clo32,
-                          const __grid_constant__ CUtensorMap tm_w, const Gemm2Args g) {
+                          const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_y,
+                          const Gemm2Args g) {
   grid_dep_wait();
   grid_dep_trigger();
   extern __shared__ uint8_t smem_raw[];
@@ -508,6 +488,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tm_chi32);
     tma_prefetch_desc(&tm_clo32);
     tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_y);
   }
   if (warp == 1) tmem_alloc(tmem_holder, 512);
   tc_fence_before();
@@ -646,34 +627,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       if (live) {
-        // Each lane holds one row's 128 columns.  Stored lane-per-row, every
-        // 16-byte store of a warp lands in a different row (32 scattered
-        // sectors per instruction).  An 8x8 transpose of float4s inside each
-        // group of 8 lanes turns that into lane-per-column, so one store
-        // instruction writes four whole 128-byte row segments.
+        // y rows leave through TMA stores: each round the warp writes a 32-row x
+        // 32-column fp32 tile (this lane = one row) into its 128-byte-swizzled
+        // staging buffer, and one lane stores it to y; the buffer is rewritten
+        // only after the previous store has read it.  Rows of the tile beyond
+        // nrows are padding rows of this tile, which nothing reads.
         const float w = row < nrows ? g.slot_weight[row0 + row] : 0.f;
-        const int gl = lane & 7;
-        const int r_base = q * 32 + (lane & ~7);  // first row of this lane's group
-        float* ybase = g.y + static_cast<size_t>(row0) * kH + nb2 * 256 + h * 128;
+        uint8_t* stg = smem + G2_OFF_STG + pw * G2_STG_WARP;
+        const int xcol = nb2 * 256 + h * 128;
 #pragma unroll
         for (int m = 0; m < 4; ++m) {
-          float4 v[8];
+          if (lane == 0) bulk_wait_group_read0();
+          __syncwarp();
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const float2 p0 = acc[16 * m + 2 * j], p1 = acc[16 * m + 2 * j + 1];
-            v[j] = make_float4(p0.x * w, p0.y * w, p1.x * w, p1.y * w);
+            *reinterpret_cast<float4*>(stg + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+                make_float4(p0.x * w, p0.y * w, p1.x * w, p1.y * w);
           }
-          transpose8_f4(v, gl);
-          // v[j] = float4 (8m + gl) of row r_base + j
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int r = r_base + j;
-            if (r < nrows) reinterpret_cast<float4*>(ybase + static_cast<size_t>(r) * kH)[8 * m + gl] = v[j];
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tm_y, xcol + 32 * m, row0 + q * 32, stg);
+            bulk_commit_group();
           }
         }
       }
       cur = nxt;
     }
+    if (lane == 0) bulk_wait_group0();  // this warp's y stores are complete before the CTA can exit
   }
 
   tc_fence_before();
@@ -742,9 +724,10 @@ cudaError_t launch_swiglu_quant(const Gemm1Args& g, int grid, cudaStream_t s) {
 }
 
 cudaError_t launch_gemm2(const CUtensorMap& tm_chi, const CUtensorMap& tm_clo, const CUtensorMap& tm_chi32,
-                         const CUtensorMap& tm_clo32, const CUtensorMap& tm_w2, const Gemm2Args& args, int grid,
-                         cudaStream_t s) {
-  return launch_chained(gemm2_weighted_kernel, dim3(grid), dim3(kThreads), G2_SMEM, s, tm_chi, tm_clo, tm_chi32, tm_clo32, tm_w2, args);
+                         const CUtensorMap& tm_clo32, const CUtensorMap& tm_w2, const CUtensorMap& tm_y,
+                         const Gemm2Args& args, int grid, cudaStream_t s) {
+  return launch_chained(gemm2_weighted_kernel, dim3(grid), dim3(kThreads), G2_SMEM, s, tm_chi, tm_clo, tm_chi32,
+                        tm_clo32, tm_w2, tm_y, args);
 }
 
 }  // namespace kf

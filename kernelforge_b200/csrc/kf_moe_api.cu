@@ -122,15 +122,16 @@ int ensure_device(int* num_sms, int* pair_clusters = nullptr) {
   return d.status;
 }
 
-// Row-major [outer, inner] bytes, box [box_outer, box_inner], 128-byte swizzle.
-bool encode_u8_2d_uncached(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
-                           uint32_t box_outer) {
+// Row-major [outer, inner] elements of 1 (u8) or 4 (f32) bytes, box [box_outer, box_inner], 128-byte swizzle.
+bool encode_2d_uncached(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner, uint64_t outer,
+                        uint32_t box_inner, uint32_t box_outer) {
   const cuuint64_t dims[2] = {inner, outer};
-  const cuuint64_t strides[1] = {inner};
+  const cuuint64_t strides[1] = {inner * static_cast<uint64_t>(elem_bytes)};
   const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t elem_strides[2] = {1, 1};
-  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
-                              elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+  const CUresult r = g_encode(map, elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT8,
+                              2, const_cast<void*>(base), dims, strides, box, elem_strides,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -139,6 +140,7 @@ bool encode_u8_2d_uncached(CUtensorMap* map, const void* base, uint64_t inner, u
 // weights and workspace reuse the encoded maps.
 struct MapCacheEntry {
   const void* base;
+  int elem_bytes;
   uint64_t inner, outer;
   uint32_t box_inner, box_outer;
   CUtensorMap map;
@@ -148,23 +150,28 @@ MapCacheEntry g_maps[kMapCache];
 int g_maps_used = 0, g_maps_next = 0;
 std::mutex g_maps_mu;
 
-bool encode_u8_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
-                  uint32_t box_outer) {
+bool encode_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner, uint64_t outer,
+               uint32_t box_inner, uint32_t box_outer) {
   std::lock_guard<std::mutex> lock(g_maps_mu);
   for (int i = 0; i < g_maps_used; ++i) {
     const MapCacheEntry& c = g_maps[i];
-    if (c.base == base && c.inner == inner && c.outer == outer && c.box_inner == box_inner &&
-        c.box_outer == box_outer) {
+    if (c.base == base && c.elem_bytes == elem_bytes && c.inner == inner && c.outer == outer &&
+        c.box_inner == box_inner && c.box_outer == box_outer) {
       *map = c.map;
       return true;
     }
   }
-  if (!encode_u8_2d_uncached(map, base, inner, outer, box_inner, box_outer)) return false;
+  if (!encode_2d_uncached(map, base, elem_bytes, inner, outer, box_inner, box_outer)) return false;
   MapCacheEntry& c = g_maps[g_maps_next];
-  c = MapCacheEntry{base, inner, outer, box_inner, box_outer, *map};
+  c = MapCacheEntry{base, elem_bytes, inner, outer, box_inner, box_outer, *map};
   g_maps_next = (g_maps_next + 1) % kMapCache;
   if (g_maps_used < kMapCache) ++g_maps_used;
   return true;
+}
+
+bool encode_u8_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
+                  uint32_t box_outer) {
+  return encode_2d(map, base, 1, inner, outer, box_inner, box_outer);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -288,7 +295,9 @@ int run_experts(const Workspace& w, void* ws, const RowLayout& in, const void* w
       const int clusters = units < pair_clusters ? units : pair_clusters;
       e = launch_gemm2_pair(tm_chi, tm_clo, tm_chi32, tm_clo32, tm_w2_half, g2, 2 * clusters, s);
     } else {
-      e = launch_gemm2(tm_chi, tm_clo, tm_chi32, tm_clo32, tm_w2, g2, units < num_sms ? units : num_sms, s);
+      CUtensorMap tm_y;
+      if (!encode_2d(&tm_y, ws_ptr<float>(ws, w.y), 4, kH, w.p_cap, 32, 32)) return KF_ERR_INVALID_ARGUMENT;
+      e = launch_gemm2(tm_chi, tm_clo, tm_chi32, tm_clo32, tm_w2, tm_y, g2, units < num_sms ? units : num_sms, s);
     }
     if (e != cudaSuccess) return KF_ERR_CUDA;
   }
