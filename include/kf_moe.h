@@ -166,7 +166,11 @@ int kf_ep_dispatch(const int32_t* topk_idx, const float* topk_weight, const void
  *   kf_ep_barrier     all count rows have landed
  *   kf_ep_pack_p2p    packs each (token, destination) row (kf_ep_dispatch's
  *                     format) straight into rank d's receive buffer (peer_recv),
- *                     sources in rank order, and writes pos as kf_ep_dispatch
+ *                     sources in rank order, and writes pos as kf_ep_dispatch;
+ *                     with hidden_states_scale == NULL, hidden_states are bf16
+ *                     rows [T][7168] and every packed row is quantised on the
+ *                     way out exactly as kf_quantize_hidden would (the upstream
+ *                     quantisation fused into the dispatch)
  *   kf_ep_barrier     all rows have landed; this rank received
  *                     sum over s of counts[s][rank] rows
  *   (kf_moe_experts_packed on the received rows -> bf16 partials)

@@ -20,6 +20,7 @@
 
 #include "kf_internal.cuh"
 #include "kf_ptx.cuh"
+#include "kf_quant.cuh"
 
 namespace kf {
 
@@ -103,6 +104,10 @@ __global__ void __launch_bounds__(kMaxRanks) ep_scan_kernel(const uint4* __restr
   }
 }
 
+// kBf16In: `hidden` holds bf16 rows [T][7168] (hscale unused) and each packed
+// row is quantised on the way out (the upstream FP8 quantisation fused into the
+// dispatch); otherwise `hidden` holds the e4m3 rows and hscale their scales.
+template <bool kBf16In>
 __global__ void __launch_bounds__(256) ep_pack_kernel(const int32_t* __restrict__ topk, const float* __restrict__ topk_w,
                                                       const uint8_t* __restrict__ hidden,
                                                       const float* __restrict__ hscale, int T, int per_rank, int world,
@@ -158,14 +163,27 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const int32_t* __restrict_
       continue;
     }
     uint8_t* dst = (peer_recv ? peer_recv[d] : send_rows) + static_cast<size_t>(r.y) * kPackedRowBytes;
-    const uint4* src = reinterpret_cast<const uint4*>(hidden + static_cast<size_t>(t) * kH);
-    uint4 v[kH / 16 / 32];
-#pragma unroll
-    for (int j = 0; j < kH / 16 / 32; ++j) v[j] = src[lane + 32 * j];
-#pragma unroll
-    for (int j = 0; j < kH / 16 / 32; ++j) reinterpret_cast<uint4*>(dst)[lane + 32 * j] = v[j];
     float* dsc = reinterpret_cast<float*>(dst + kH);
-    for (int kb = lane; kb < kHB; kb += 32) dsc[kb] = hscale[static_cast<size_t>(kb) * T + t];
+    if constexpr (kBf16In) {
+      // two 128-column blocks per round: lanes 0-15 the even one, 16-31 the odd one
+      const uint4* src = reinterpret_cast<const uint4*>(hidden + static_cast<size_t>(t) * kH * 2);
+#pragma unroll 4
+      for (int i = 0; i < kHB / 2; ++i) {
+        const int kb = 2 * i + (lane >> 4);
+        float sc;
+        const uint2 q = quantize_block16(src[kb * 16 + (lane & 15)], sc);
+        reinterpret_cast<uint2*>(dst + kb * kBlk)[lane & 15] = q;
+        if ((lane & 15) == 0) dsc[kb] = sc;
+      }
+    } else {
+      const uint4* src = reinterpret_cast<const uint4*>(hidden + static_cast<size_t>(t) * kH);
+      uint4 v[kH / 16 / 32];
+#pragma unroll
+      for (int j = 0; j < kH / 16 / 32; ++j) v[j] = src[lane + 32 * j];
+#pragma unroll
+      for (int j = 0; j < kH / 16 / 32; ++j) reinterpret_cast<uint4*>(dst)[lane + 32 * j] = v[j];
+      for (int kb = lane; kb < kHB; kb += 32) dsc[kb] = hscale[static_cast<size_t>(kb) * T + t];
+    }
     if (lane < kTopK) {
       const int e = topk[static_cast<size_t>(t) * kTopK + lane];
       const bool own = e >= 0 && e < kEG && e / per_rank == d;
@@ -315,7 +333,7 @@ int kf_ep_dispatch(const int32_t* topk_idx, const float* topk_weight, const void
   const int per_rank = kEG / world;
   ep_masks_kernel<<<nchunk, 256, 0, s>>>(topk_idx, T, per_rank, world, dmasks);
   ep_scan_kernel<<<1, kMaxRanks, 0, s>>>(dmasks, nchunk, world, chunk_base, send_counts, dest_offset, nullptr, 0);
-  ep_pack_kernel<<<nchunk, 256, 0, s>>>(topk_idx, topk_weight, static_cast<const uint8_t*>(hidden_states),
+  ep_pack_kernel<false><<<nchunk, 256, 0, s>>>(topk_idx, topk_weight, static_cast<const uint8_t*>(hidden_states),
                                         hidden_states_scale, T, per_rank, world, dmasks, chunk_base, dest_offset,
                                         static_cast<uint8_t*>(send_rows), pos, nullptr, nullptr, 0, 0, nullptr);
   return cudaGetLastError() == cudaSuccess ? KF_OK : KF_ERR_CUDA;
@@ -346,17 +364,25 @@ int kf_ep_pack_p2p(const int32_t* topk_idx, const float* topk_weight, const void
   const int T = num_tokens;
   if (T < 0 || !valid_world(world) || rank < 0 || rank >= world) return KF_ERR_INVALID_ARGUMENT;
   if (T == 0) return KF_OK;
-  if (!topk_idx || !topk_weight || !hidden_states || !hidden_states_scale || !counts || !peer_recv || !pos ||
-      !status || !workspace || recv_capacity < 0)
+  if (!topk_idx || !topk_weight || !hidden_states || !counts || !peer_recv || !pos || !status || !workspace ||
+      recv_capacity < 0)
     return KF_ERR_INVALID_ARGUMENT;
   if (reinterpret_cast<uintptr_t>(hidden_states) & 15u) return KF_ERR_INVALID_ARGUMENT;
   const EpWorkspace w = plan_ep(T, world);
   if (workspace_bytes < w.total) return KF_ERR_WORKSPACE_TOO_SMALL;
   const int nchunk = (T + kChunkTokens - 1) / kChunkTokens;
-  ep_pack_kernel<<<nchunk, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      topk_idx, topk_weight, static_cast<const uint8_t*>(hidden_states), hidden_states_scale, T, kEG / world, world,
-      ws_ptr<uint4>(workspace, w.dmasks), ws_ptr<int32_t>(workspace, w.chunk_base),
-      ws_ptr<int32_t>(workspace, w.dest_offset), nullptr, pos, peer_recv, counts, rank, recv_capacity, status);
+  const int per_rank = kEG / world;
+  if (hidden_states_scale) {
+    ep_pack_kernel<false><<<nchunk, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        topk_idx, topk_weight, static_cast<const uint8_t*>(hidden_states), hidden_states_scale, T, per_rank, world,
+        ws_ptr<uint4>(workspace, w.dmasks), ws_ptr<int32_t>(workspace, w.chunk_base),
+        ws_ptr<int32_t>(workspace, w.dest_offset), nullptr, pos, peer_recv, counts, rank, recv_capacity, status);
+  } else {
+    ep_pack_kernel<true><<<nchunk, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        topk_idx, topk_weight, static_cast<const uint8_t*>(hidden_states), nullptr, T, per_rank, world,
+        ws_ptr<uint4>(workspace, w.dmasks), ws_ptr<int32_t>(workspace, w.chunk_base),
+        ws_ptr<int32_t>(workspace, w.dest_offset), nullptr, pos, peer_recv, counts, rank, recv_capacity, status);
+  }
   return cudaGetLastError() == cudaSuccess ? KF_OK : KF_ERR_CUDA;
 }
 

@@ -13,6 +13,7 @@
 #include <cuda_runtime.h>
 
 #include "kf_internal.cuh"
+#include "kf_quant.cuh"
 
 namespace kf {
 namespace {
@@ -22,30 +23,8 @@ constexpr int kPairsPerWarp = 4;  // block pairs per warp: four 16-byte loads in
 
 __device__ __forceinline__ void quantize_pair(uint4 raw, int lane, uint8_t* __restrict__ q, float* __restrict__ scale,
                                               size_t base, size_t scale_idx) {
-  const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
-  float v[8];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __bfloat1622float2(h2[i]);
-    v[2 * i] = f.x;
-    v[2 * i + 1] = f.y;
-  }
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
-#pragma unroll
-  for (int off = 8; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-  const float s = amax > 0.f ? __fdiv_rn(amax, 448.0f) : 1.0f;
-  uint32_t w[2];
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(
-        make_float2(__fdiv_rn(v[4 * i], s), __fdiv_rn(v[4 * i + 1], s)), __NV_SATFINITE, __NV_E4M3);
-    const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(
-        make_float2(__fdiv_rn(v[4 * i + 2], s), __fdiv_rn(v[4 * i + 3], s)), __NV_SATFINITE, __NV_E4M3);
-    w[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
-  }
-  *reinterpret_cast<uint2*>(q + base) = make_uint2(w[0], w[1]);
+  float s;
+  *reinterpret_cast<uint2*>(q + base) = quantize_block16(raw, s);
   if ((lane & 15) == 0) scale[scale_idx] = s;
 }
 

@@ -206,6 +206,12 @@ class ExpertParallelMoE:
         return int(((ids >= 0) & (loc >= 0) & (loc < self.num_local)).sum().item())
 
     def forward(self, routing_logits, routing_bias, hidden_states, hidden_states_scale, routed_scaling_factor):
+        """The layer on this rank's tokens.  ``hidden_states`` are e4m3 with ``hidden_states_scale``
+        ``[56, T]``, or bf16 rows with ``hidden_states_scale=None``: then the peer exchange quantises
+        each row as it packs it (the other plumbings quantise the rows first)."""
+        if hidden_states_scale is None and self.plumbing != "p2p":
+            from . import binding as B
+            hidden_states, hidden_states_scale = B.quantize_hidden(hidden_states)
         if self.plumbing == "p2p":
             return self._forward_p2p(routing_logits, routing_bias, hidden_states, hidden_states_scale,
                                      routed_scaling_factor)
@@ -248,7 +254,9 @@ class ExpertParallelMoE:
                                       self.group, dev)
         idx, w = self.route_fn(routing_logits, routing_bias, routed_scaling_factor)
         hid = hidden_states.contiguous()
-        hs = hidden_states_scale.contiguous()
+        hs = hidden_states_scale.contiguous() if hidden_states_scale is not None else None
+        if hs is None and hid.dtype != torch.bfloat16:
+            raise ValueError("without hidden_states_scale, hidden_states must be bf16 rows")
         stream = torch.cuda.current_stream(dev).cuda_stream
         ws = B._ep_workspace(dev, int(lib.kf_ep_workspace_bytes(T, world)))
         sz = ctypes.c_size_t(ws.numel())

@@ -71,11 +71,20 @@ def _ptrs(ts):
     return torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64, device="cuda")
 
 
-def _emulated_ranks(world, T):
+def _emulated_ranks_from(world, T, fp8_rows):
+    """As _emulated_ranks, with each rank's hidden rows replaced by the given (e4m3, scales)."""
+    return _emulated_ranks(world, T, fp8_rows=fp8_rows)
+
+
+def _emulated_ranks(world, T, bf16_rows=None, fp8_rows=None):
     lib = B.library()
     ranks = []
     for r in range(world):
         ti = to_cuda(S.token_inputs(T, seed=200 + r))
+        if bf16_rows is not None:       # pack bf16 rows, quantised on the way out
+            ti = S.TokenInputs(ti.routing_logits, ti.routing_bias, bf16_rows[r], None)
+        if fp8_rows is not None:
+            ti = S.TokenInputs(ti.routing_logits, ti.routing_bias, fp8_rows[r][0], fp8_rows[r][1])
         idx, w = B.route(ti.routing_logits, ti.routing_bias, 2.5)
         ranks.append({"ti": ti, "idx": idx, "w": w,
                       "counts": torch.zeros(world * world, dtype=torch.int32, device="cuda"),
@@ -123,6 +132,24 @@ def test_peer_pack_matches_dispatch(world):
             parts.append(sends[s][0][off:off + int(counts[s, d])])
         expect = torch.cat(parts)
         assert torch.equal(x["recv"][:expect.shape[0]], expect)
+
+
+def test_peer_pack_quantises_bf16_rows_like_the_quantiser():
+    """bf16 rows packed with the quantisation fused in = the rows kf_quantize_hidden makes, packed as e4m3."""
+    world, T = 4, 300
+    g = torch.Generator().manual_seed(9)
+    rows = [(torch.randn(T, B.H, generator=g) * 3).to(torch.bfloat16).cuda() for _ in range(world)]
+    fused = _emulated_ranks(world, T, bf16_rows=rows)
+    plain = []
+    for r in range(world):           # the same routing inputs, rows quantised first
+        q, s = B.quantize_hidden(rows[r])
+        plain.append((q, s))
+    ref = _emulated_ranks_from(world, T, plain)
+    for d, (a, b) in enumerate(zip(fused, ref)):
+        assert torch.equal(a["counts"], b["counts"])
+        n = int(a["counts"].view(world, world)[:, d].sum())
+        assert n > 0 and torch.equal(a["recv"][:n], b["recv"][:n])
+        assert torch.equal(a["pos"], b["pos"])
 
 
 def test_peer_return_fused_into_reduce():
