@@ -1,4 +1,4 @@
-"""Expert-parallel MoE layer: 256 experts sharded over N GPUs, NCCL all-to-all dispatch/combine.
+"""Expert-parallel MoE layer: 256 experts sharded over N GPUs, peer-memory (or NCCL) dispatch/combine.
 
 Rank r owns global experts ``[r*256/N, (r+1)*256/N)`` (``local_expert_offset``
 in the reference's data contract, ``solution/triton/kernel.py:1826``; the
@@ -10,17 +10,18 @@ the CUDA routing kernel, then:
    reaches at most ``topk_group`` = 4 ranks).  A dispatched row carries the FP8
    hidden row, its 56 fp32 scales and the token's 8 (expert id, weight) pairs
    with the experts the receiver does not own masked to -1 (7456 bytes);
-2. the receiver runs the grouped expert kernels (``kf_moe_experts``) on the
-   rows it got, producing one partial sum per row;
-3. combine: partials travel back along the reverse all-to-all and each token's
-   output is the sum of its partials in ascending source-rank order (fixed
-   order, no atomics), rounded to bf16 once.
+2. the receiver runs the grouped expert kernels (``kf_moe_experts_packed``) on
+   the rows it got, producing one partial sum per row;
+3. combine: the partials travel back to their sources and each token's output
+   is the sum of its partials in ascending rank order (fixed order, no
+   atomics), rounded to bf16 once.
 
 By default the rows and the partials move by stores into the ranks' symmetric
 buffers (``PeerExchange``): the pack kernel writes each row straight into its
 destination's receive area and the expert stage's reduce kernel writes each
 partial back into its source's return area, with the library's bounded barrier
-between the phases; reading the count matrix is the one host synchronisation of a step.
+between the phases; reading the count matrix is the one host synchronisation
+of a step.
 With ``plumbing="cuda"`` the same kernels run around ``torch.distributed``
 all-to-alls over NCCL (split sizes first, then rows).  The tensor-op functions
 below restate the data flow for the CPU tests.
