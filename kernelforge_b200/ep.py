@@ -153,6 +153,17 @@ class PeerExchange:
         B._check(rc, "kf_ep_barrier")
 
 
+def peer_capacity_needs(counts: torch.Tensor):
+    """Rows the largest receive area and the largest return area must hold for a step.
+
+    ``counts[s, d]`` = rows source s sends to destination d (every rank holds
+    the same matrix after the first barrier, so every rank computes the same
+    answer).  Receive area of d: the sum of column d; return area of s: the sum
+    of row s.
+    """
+    return int(counts.sum(0).max()), int(counts.sum(1).max())
+
+
 def _exchange_counts(send_counts: torch.Tensor, group) -> torch.Tensor:
     recv = torch.empty_like(send_counts)
     dist.all_to_all_single(recv, send_counts, group=group)
@@ -274,7 +285,7 @@ class ExpertParallelMoE:
 
         counts = plan(self._peer)
         # every rank holds the same count matrix, so all of them take this branch together
-        need_recv, need_send = int(counts.sum(0).max()), int(counts.sum(1).max())
+        need_recv, need_send = peer_capacity_needs(counts)
         if need_recv > self._peer.recv_cap or need_send > self._peer.send_cap:
             self._peer = PeerExchange(max(need_recv, self._peer.recv_cap), max(need_send, self._peer.send_cap),
                                       world, rank, self.group, dev)

@@ -94,3 +94,11 @@ def test_ep_dropped_rank_raises_on_survivor(tmp_path):
     res = _run(2, [16, 16], mode="drop", tmp_path=tmp_path)
     assert res[1].get("dropped")
     assert "error" in res[0]
+
+
+def test_peer_capacity_needs():
+    """Receive-area need = the largest column sum, return-area need = the largest row sum of the count matrix."""
+    from kernelforge_b200.ep import peer_capacity_needs
+    counts = torch.tensor([[5, 0, 7], [1, 2, 3], [0, 9, 0]], dtype=torch.int32)   # [source, destination]
+    assert peer_capacity_needs(counts) == (11, 12)   # column 1: 0+2+9, row 0: 5+0+7
+    assert peer_capacity_needs(torch.zeros(2, 2, dtype=torch.int32)) == (0, 0)
