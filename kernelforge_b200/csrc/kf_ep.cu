@@ -13,6 +13,15 @@
 // Combine sums, per token, the partial rows returned by its destinations in
 // ascending rank order (fp32), with one bf16 rounding: no atomics, fixed order.
 //
+// The rows and partials travel either through NCCL all-to-alls (kf_ep_dispatch
+// packs into a local send buffer) or by plain stores into the other ranks'
+// symmetric buffers: kf_ep_plan_p2p publishes this rank's per-destination
+// counts into every rank's count matrix, kf_ep_pack_p2p stores each packed row
+// (optionally quantising bf16 rows on the way) straight into its destination's
+// receive area, the expert stage's reduce (or kf_ep_return_p2p) stores each
+// partial back into its source's return area, and kf_ep_barrier separates the
+// phases with a bounded wait.
+//
 // The reference has no multi-GPU path; these kernels serve the expert-parallel
 // layer built around its data contract (local_expert_offset, kernel.py:1826).
 #include <cuda_bf16.h>
