@@ -44,6 +44,12 @@ extern "C" {
 #define KF_MOE_TOPK_GROUP 4
 #define KF_MOE_BLOCK 128
 
+/* Largest num_tokens / num_rows any entry point accepts (larger values are
+ * KF_ERR_INVALID_ARGUMENT, and the size queries return 0).  It keeps every row
+ * count, tile count and workspace offset inside 32-bit indexes; the workspace of
+ * such a call would already be terabytes, far beyond one GPU's memory. */
+#define KF_MOE_MAX_TOKENS (1 << 24)
+
 /* Host-side return codes. */
 #define KF_OK 0
 #define KF_ERR_INVALID_ARGUMENT 1
@@ -182,7 +188,11 @@ int kf_ep_dispatch(const int32_t* topk_idx, const float* topk_weight, const void
  * Every rank's receive area holds recv_capacity rows (the same on all ranks; a
  * row beyond it is dropped and sets KF_STATUS_SLOT_OVERFLOW in *status), which
  * the caller sizes from the complete count matrix available after the first
- * barrier.  counts is this rank's own (complete) count matrix.  The barrier stores `epoch`
+ * barrier.  counts is this rank's own (complete) count matrix.  The return
+ * (kf_ep_return_p2p, kf_moe_experts_packed_p2p) stores only the first
+ * sum over s of counts[s][rank] rows: rows past that total have no position in
+ * any source's send order, so a num_rows larger than the total never writes
+ * into a peer's buffer outside that source's own rows.  The barrier stores `epoch`
  * (one more than the previous barrier's) into slot `rank` of every rank's int32
  * flag array (peer_flags; zeroed before the first barrier) and waits, bounded,
  * until its own flags (my_flags) all reach it; a rank that does not arrive sets

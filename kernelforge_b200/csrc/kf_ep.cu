@@ -228,7 +228,9 @@ __global__ void __launch_bounds__(256) ep_return_kernel(const __nv_bfloat16* __r
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const int warps = gridDim.x * (blockDim.x >> 5);
-  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < R; r += warps) {
+  // rows past the received total have no place in any source's send order
+  const int rows = R < recv_off[world] ? R : recv_off[world];
+  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
     int s = 0;
     while (s + 1 < world && recv_off[s + 1] <= r) ++s;
     const size_t dst_row = static_cast<size_t>(send_off[s]) + (r - recv_off[s]);
@@ -312,12 +314,12 @@ using namespace kf;
 extern "C" {
 
 size_t kf_ep_workspace_bytes(int32_t num_tokens, int32_t world) {
-  if (num_tokens < 0 || !valid_world(world)) return 0;
+  if (!valid_tokens(num_tokens) || !valid_world(world)) return 0;
   return plan_ep(num_tokens, world).total;
 }
 
 int32_t kf_ep_max_send_rows(int32_t num_tokens, int32_t world) {
-  if (num_tokens < 0 || !valid_world(world)) return 0;
+  if (!valid_tokens(num_tokens) || !valid_world(world)) return 0;
   return num_tokens * (world < kMaxDestPerToken ? world : kMaxDestPerToken);
 }
 
@@ -325,7 +327,7 @@ int kf_ep_dispatch(const int32_t* topk_idx, const float* topk_weight, const void
                    const float* hidden_states_scale, int32_t num_tokens, int32_t world, void* send_rows,
                    int64_t* send_counts, int32_t* pos, void* workspace, size_t workspace_bytes, void* stream) {
   const int T = num_tokens;
-  if (T < 0 || !valid_world(world)) return KF_ERR_INVALID_ARGUMENT;
+  if (!valid_tokens(T) || !valid_world(world)) return KF_ERR_INVALID_ARGUMENT;
   if (!send_counts) return KF_ERR_INVALID_ARGUMENT;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (T == 0) return cudaMemsetAsync(send_counts, 0, sizeof(int64_t) * world, s) == cudaSuccess ? KF_OK : KF_ERR_CUDA;
@@ -351,7 +353,7 @@ int kf_ep_dispatch(const int32_t* topk_idx, const float* topk_weight, const void
 int kf_ep_plan_p2p(const int32_t* topk_idx, int32_t num_tokens, int32_t world, int32_t rank,
                    int32_t* const* peer_counts, void* workspace, size_t workspace_bytes, void* stream) {
   const int T = num_tokens;
-  if (T < 0 || !valid_world(world) || rank < 0 || rank >= world || !peer_counts || !workspace)
+  if (!valid_tokens(T) || !valid_world(world) || rank < 0 || rank >= world || !peer_counts || !workspace)
     return KF_ERR_INVALID_ARGUMENT;
   if (T > 0 && !topk_idx) return KF_ERR_INVALID_ARGUMENT;
   const EpWorkspace w = plan_ep(T, world);
@@ -371,7 +373,7 @@ int kf_ep_pack_p2p(const int32_t* topk_idx, const float* topk_weight, const void
                    const int32_t* counts, uint8_t* const* peer_recv, int32_t recv_capacity, int32_t* pos,
                    int32_t* status, void* workspace, size_t workspace_bytes, void* stream) {
   const int T = num_tokens;
-  if (T < 0 || !valid_world(world) || rank < 0 || rank >= world) return KF_ERR_INVALID_ARGUMENT;
+  if (!valid_tokens(T) || !valid_world(world) || rank < 0 || rank >= world) return KF_ERR_INVALID_ARGUMENT;
   if (T == 0) return KF_OK;
   if (!topk_idx || !topk_weight || !hidden_states || !counts || !peer_recv || !pos || !status || !workspace ||
       recv_capacity < 0)
@@ -397,7 +399,7 @@ int kf_ep_pack_p2p(const int32_t* topk_idx, const float* topk_weight, const void
 
 int kf_ep_return_p2p(const void* partials, int32_t num_rows, int32_t world, int32_t rank, const int32_t* counts,
                      void* const* peer_back, void* stream) {
-  if (num_rows < 0 || !valid_world(world) || rank < 0 || rank >= world) return KF_ERR_INVALID_ARGUMENT;
+  if (!valid_tokens(num_rows) || !valid_world(world) || rank < 0 || rank >= world) return KF_ERR_INVALID_ARGUMENT;
   if (num_rows == 0) return KF_OK;
   if (!partials || !counts || !peer_back || (reinterpret_cast<uintptr_t>(partials) & 15u))
     return KF_ERR_INVALID_ARGUMENT;
@@ -419,7 +421,7 @@ int kf_ep_barrier(int32_t* const* peer_flags, const int32_t* my_flags, int32_t r
 
 int kf_ep_combine(const void* partials, int32_t partials_fp32, const int32_t* pos, int32_t num_tokens,
                   int32_t world, void* output, void* stream) {
-  if (num_tokens < 0 || !valid_world(world)) return KF_ERR_INVALID_ARGUMENT;
+  if (!valid_tokens(num_tokens) || !valid_world(world)) return KF_ERR_INVALID_ARGUMENT;
   if (num_tokens == 0) return KF_OK;
   if (!pos || !output) return KF_ERR_INVALID_ARGUMENT;
   if ((reinterpret_cast<uintptr_t>(output) & 15u) || (partials && (reinterpret_cast<uintptr_t>(partials) & 15u)))

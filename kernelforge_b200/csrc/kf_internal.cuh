@@ -21,6 +21,9 @@ constexpr int kIB = kI / kBlk;                // 16 K-blocks of the intermediate
 constexpr int kChunkTokens = 128;             // tokens per routing/permute chunk (4 x 32-bit masks)
 constexpr int kMaxLocalExperts = 256;
 
+// Token / row counts every entry point accepts: [0, KF_MOE_MAX_TOKENS].
+inline bool valid_tokens(int32_t n) { return n >= 0 && n <= KF_MOE_MAX_TOKENS; }
+
 // silu(x) = x * sigmoid(x) for the SwiGLU epilogues, with the hardware exp2 and
 // reciprocal approximations (a few ulp; the reference's Triton sigmoid is of the
 // same class).  Returns 0 when exp(-x) overflows, so large negative gates never

@@ -177,7 +177,7 @@ bool encode_u8_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t o
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 int check_common(int32_t T, int32_t E, int32_t offset) {
-  if (T < 0 || E < 1 || E > kMaxLocalExperts) return KF_ERR_INVALID_ARGUMENT;
+  if (!valid_tokens(T) || E < 1 || E > kMaxLocalExperts) return KF_ERR_INVALID_ARGUMENT;
   if (offset < 0 || offset + E > kEG) return KF_ERR_INVALID_ARGUMENT;
   return KF_OK;
 }
@@ -384,7 +384,7 @@ using namespace kf;
 extern "C" {
 
 size_t kf_moe_workspace_bytes(int32_t num_tokens, int32_t num_local_experts) {
-  if (num_tokens < 0 || num_local_experts < 1 || num_local_experts > kMaxLocalExperts) return 0;
+  if (!valid_tokens(num_tokens) || num_local_experts < 1 || num_local_experts > kMaxLocalExperts) return 0;
   return plan_workspace(num_tokens, num_local_experts).total;
 }
 
@@ -406,7 +406,7 @@ const char* kf_moe_error_string(int code) {
 
 int kf_moe_route(const float* routing_logits, const void* routing_bias, int32_t num_tokens,
                  float routed_scaling_factor, int32_t* topk_idx, float* topk_weight, void* stream) {
-  if (num_tokens < 0) return KF_ERR_INVALID_ARGUMENT;
+  if (!valid_tokens(num_tokens)) return KF_ERR_INVALID_ARGUMENT;
   if (num_tokens == 0) return KF_OK;
   if (!routing_logits || !routing_bias || !topk_idx || !topk_weight) return KF_ERR_INVALID_ARGUMENT;
   if (!aligned16(routing_logits) || !aligned16(routing_bias)) return KF_ERR_INVALID_ARGUMENT;

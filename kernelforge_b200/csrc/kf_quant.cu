@@ -57,7 +57,7 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_rows_kernel(const __nv
 }  // namespace kf
 
 extern "C" int kf_quantize_hidden(const void* x, int32_t num_tokens, void* out, float* out_scale, void* stream) {
-  if (num_tokens < 0 || (num_tokens > 0 && (!x || !out || !out_scale))) return KF_ERR_INVALID_ARGUMENT;
+  if (!kf::valid_tokens(num_tokens) || (num_tokens > 0 && (!x || !out || !out_scale))) return KF_ERR_INVALID_ARGUMENT;
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15u) return KF_ERR_INVALID_ARGUMENT;
   if (num_tokens == 0) return KF_OK;
   const long long warps = (static_cast<long long>(num_tokens) * (kf::kHB / 2) + kf::kPairsPerWarp - 1) / kf::kPairsPerWarp;

@@ -509,7 +509,9 @@ __global__ void __launch_bounds__(256) unpermute_reduce_kernel(const int32_t* __
   __shared__ __nv_bfloat16* peer_row;
   if (po.peer_back) {
     // received row t came from source s (sources in rank order) as its j-th row
-    // for this rank; it returns to row (s's rows for lower ranks) + j of s's buffer
+    // for this rank; it returns to row (s's rows for lower ranks) + j of s's buffer.
+    // A row past the received total (T larger than the count matrix says) has no
+    // place in any source's send order and is not stored.
     if (threadIdx.x == 0) {
       int s = 0, off = 0;
       while (s + 1 < po.world && off + po.counts[s * po.world + po.rank] <= t) {
@@ -518,9 +520,12 @@ __global__ void __launch_bounds__(256) unpermute_reduce_kernel(const int32_t* __
       }
       int so = 0;
       for (int d = 0; d < po.rank; ++d) so += po.counts[s * po.world + d];
-      peer_row = static_cast<__nv_bfloat16*>(po.peer_back[s]) + (static_cast<size_t>(so) + (t - off)) * kH;
+      peer_row = t - off < po.counts[s * po.world + po.rank]
+                     ? static_cast<__nv_bfloat16*>(po.peer_back[s]) + (static_cast<size_t>(so) + (t - off)) * kH
+                     : nullptr;
     }
     __syncthreads();
+    if (peer_row == nullptr) return;  // uniform over the block
   }
   int sl[8];
   int n = 0;

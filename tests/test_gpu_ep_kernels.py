@@ -175,6 +175,46 @@ def test_peer_return_fused_into_reduce():
         assert torch.equal(x["back"][:expect.shape[0]], expect)
 
 
+@pytest.mark.parametrize("fused", [True, False])
+def test_peer_return_stores_nothing_past_the_received_rows(fused):
+    """A call with more rows than the count matrix gives this rank: the extra rows
+    (no local pair) reach no source's return buffer, fused into the reduce or not."""
+    world, T, d = 2, 300, 0
+    E = 256 // world
+    lib = B.library()
+    ranks = _emulated_ranks(world, T)
+    counts = ranks[0]["counts"].cpu().view(world, world)
+    R = int(counts[:, d].sum())
+    extra = min(16, T * world - R)
+    assert extra > 0
+    x = ranks[d]
+    ids = x["recv"][R:R + extra, B.H + 56 * 4:B.H + 56 * 4 + 32]
+    ids.fill_(0xFF)                       # expert ids -1: rows without a local pair
+    rows = x["recv"][:R + extra]
+    wb = gpu_bank(E, d * E, seed=5)
+    part = B.experts_packed(rows[:R], wb.gemm1_weights, wb.gemm1_weights_scale, wb.gemm2_weights,
+                            wb.gemm2_weights_scale, d * E)
+    for y in ranks:
+        y["back"].fill_(7.0)
+    peer_back = _ptrs([y["back"] for y in ranks])
+    if fused:
+        B.experts_packed_p2p(rows, wb.gemm1_weights, wb.gemm1_weights_scale, wb.gemm2_weights,
+                             wb.gemm2_weights_scale, d * E, x["counts"], d, world, peer_back)
+    else:
+        part_x = B.experts_packed(rows, wb.gemm1_weights, wb.gemm1_weights_scale, wb.gemm2_weights,
+                                  wb.gemm2_weights_scale, d * E)
+        rc = lib.kf_ep_return_p2p(B._ptr(part_x), R + extra, world, d, x["counts"].data_ptr(), peer_back.data_ptr(),
+                                  torch.cuda.current_stream().cuda_stream)
+        assert rc == 0
+    torch.cuda.synchronize()
+    assert B.read_status() == 0
+    for s, y in enumerate(ranks):
+        n, so = int(counts[s, d]), int(counts[s, :d].sum())
+        off = int(counts[:s, d].sum())
+        assert torch.equal(y["back"][so:so + n], part[off:off + n])
+        assert bool((y["back"][:so] == 7.0).all()) and bool((y["back"][so + n:] == 7.0).all())
+
+
 def test_peer_barrier_times_out_instead_of_hanging():
     """A rank that never arrives: the barrier gives up after its bounded wait and reports it (no trap, no hang)."""
     lib = B.library()

@@ -48,6 +48,25 @@ def test_workspace_bytes_is_host_only_and_monotone():
     assert b > rows * (7168 + 2 * 2048 + 7168 * 4)
 
 
+def test_token_ceiling():
+    """Counts above KF_MOE_MAX_TOKENS are refused on the host (no 32-bit index can wrap)."""
+    text = open(os.path.join(ROOT, "include", "kf_moe.h")).read()
+    m = re.search(r"#define KF_MOE_MAX_TOKENS \(1 << (\d+)\)", text)
+    cap = 1 << int(m.group(1))
+    lib = B.library()
+    assert lib.kf_moe_workspace_bytes(cap, 256) >= lib.kf_moe_workspace_bytes(cap - 1, 256) > 0
+    assert lib.kf_moe_workspace_bytes(cap + 1, 32) == 0
+    assert lib.kf_moe_workspace_bytes(2 ** 31 - 1, 1) == 0
+    assert lib.kf_ep_max_send_rows(cap, 8) == cap * 8
+    assert lib.kf_ep_max_send_rows(cap + 1, 8) == 0
+    assert lib.kf_ep_workspace_bytes(cap + 1, 8) == 0
+    null = ctypes.c_void_p(0)
+    rc = lib.kf_moe_forward(null, null, null, null, null, null, null, null, cap + 1, 32, 0, ctypes.c_float(1.0), null,
+                            null, ctypes.c_size_t(0), null)
+    assert rc == 1
+    assert lib.kf_quantize_hidden(null, cap + 1, null, null, null) == 1
+
+
 def test_error_strings():
     lib = B.library()
     assert lib.kf_moe_error_string(0) == b"ok"
