@@ -21,7 +21,7 @@ INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libkf_moe.so")
 SOURCES = ["kf_route_permute.cu", "kf_grouped_gemm.cu", "kf_grouped_gemm_pair.cu", "kf_moe_api.cu",
            "kf_moe_noalloc.cu", "kf_ep.cu", "kf_quant.cu"]
-HEADERS = ["kf_ptx.cuh", "kf_internal.cuh", "kf_quant.cuh"]
+HEADERS = ["kf_ptx.cuh", "kf_internal.cuh", "kf_quant.cuh", "kf_fp8.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xptxas", "-v", f"-I{INCLUDE}"]
