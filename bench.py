@@ -2,15 +2,17 @@
 """Benchmark of the fused DeepSeek-V3 FP8 block-scale MoE layer on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kernelforge|reference]
-                    [--workload ep|prefill|decode] [--tokens T]
+                    [--workload ep|prefill|decode] [--tokens T] [--zipf] [--graph]
+                    [--ep-exchange p2p|nccl] [--no-cpu-baseline]
 
 Default workload ("ep", the layer of config 3 of the headline metric): 8192
 tokens per GPU, all 256 experts sharded 256/N per GPU (N=1: all 256 on one GPU),
 hidden 7168 / intermediate 2048 FP8 block-scaled weights; tokens are routed over
 all experts.  With N > 1 the layer runs expert-parallel (one process per GPU,
-launched by torchrun) with NCCL all-to-all dispatch/combine.  A "step" is one
-forward of the layer over the GPU's 8192 tokens; per-GPU work is fixed as N
-grows (weak scaling).
+launched by torchrun): dispatch rows and returned partials travel by stores into
+the ranks' symmetric buffers (--ep-exchange p2p, the default) or by NCCL
+all-to-all (--ep-exchange nccl).  A "step" is one forward of the layer over the
+GPU's 8192 tokens; per-GPU work is fixed as N grows (weak scaling).
 
 Prints ONE JSON line (rank 0).  Metric: tokens/s of the whole job (all GPUs).
 Inputs are synthetic (seeded N(0,1) logits / activations, N(0,0.02) weights,
