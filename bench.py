@@ -368,6 +368,14 @@ def main():
     e2e = {"value": world * T * e2e_steps / (e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
            "d2h_bytes_per_step": d2h, "steps": e2e_steps, "copy_ms_per_step_serial": c0.elapsed_time(c1),
            "overlap": "each step's host copies run on side streams beside the neighbouring steps' kernels"}
+    if world > 1:
+        # a barrier of the peer exchange that gave up in the last step invalidates the numbers; every
+        # rank reads its own status word and all of them raise together
+        st = torch.tensor([layer.status()], dtype=torch.int64, device=dev)
+        torch.distributed.all_reduce(st, op=torch.distributed.ReduceOp.MAX)
+        err = ep.peer_status_error(int(st.item()))
+        if err:
+            raise RuntimeError(err)
 
     # roofline of the dominant kernel (GEMM1: 2/3 of the layer's FLOPs)
     g1_ms, g1_n = prof["gemm1_swiglu"]

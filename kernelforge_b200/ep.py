@@ -164,6 +164,24 @@ def peer_capacity_needs(counts: torch.Tensor):
     return int(counts.sum(0).max()), int(counts.sum(1).max())
 
 
+STATUS_SLOT_OVERFLOW = 0x10   # KF_STATUS_SLOT_OVERFLOW: a row beyond a receive area was dropped
+STATUS_TIMEOUT_PEER = 0x20    # KF_STATUS_TIMEOUT_PEER: a rank did not reach a barrier in time
+
+
+def peer_status_error(status: int) -> Optional[str]:
+    """The error a non-zero status word of the peer exchange stands for (None for 0)."""
+    if not status:
+        return None
+    what = []
+    if status & STATUS_TIMEOUT_PEER:
+        what.append("a rank did not reach a barrier in time")
+    if status & STATUS_SLOT_OVERFLOW:
+        what.append("a receive area overflowed")
+    if status & ~(STATUS_TIMEOUT_PEER | STATUS_SLOT_OVERFLOW):
+        what.append("unknown bits")
+    return f"peer exchange: device status {status:#x} ({'; '.join(what)})"
+
+
 def _exchange_counts(send_counts: torch.Tensor, group) -> torch.Tensor:
     recv = torch.empty_like(send_counts)
     dist.all_to_all_single(recv, send_counts, group=group)
@@ -217,10 +235,30 @@ class ExpertParallelMoE:
         loc = ids.to(torch.int64) - self.offset
         return int(((ids >= 0) & (loc >= 0) & (loc < self.num_local)).sum().item())
 
+    def check(self) -> None:
+        """Raise ``RuntimeError`` if a device-side check of the peer exchange has failed: a barrier
+        that gave up waiting for a rank, or a row dropped at a full receive area.  Synchronises with
+        the device.  ``forward`` runs the same check when it reads the next step's count matrix, so a
+        failure in a step's pack or return barrier surfaces one step later at the latest; calling
+        this after a step reports it at once.  The status is sticky: once set, every later step
+        raises, since the exchange can no longer be trusted.  No-op for the NCCL and CPU plumbings
+        (their collectives raise their own errors)."""
+        err = peer_status_error(self.status())
+        if err:
+            raise RuntimeError(err)
+
+    def status(self) -> int:
+        """The peer exchange's device status word (0: no failure; synchronises), 0 for other plumbings."""
+        if self.plumbing != "p2p" or self._peer is None:
+            return 0
+        return int(self._peer.status.item())
+
     def forward(self, routing_logits, routing_bias, hidden_states, hidden_states_scale, routed_scaling_factor):
         """The layer on this rank's tokens.  ``hidden_states`` are e4m3 with ``hidden_states_scale``
         ``[56, T]``, or bf16 rows with ``hidden_states_scale=None``: then the peer exchange quantises
-        each row as it packs it (the other plumbings quantise the rows first)."""
+        each row as it packs it (the other plumbings quantise the rows first).  With the peer
+        exchange, a failed barrier of this step's later phases raises at the next step or at
+        ``check()``."""
         if hidden_states_scale is None and self.plumbing != "p2p":
             from . import binding as B
             hidden_states, hidden_states_scale = B.quantize_hidden(hidden_states)
@@ -278,9 +316,9 @@ class ExpertParallelMoE:
                                         stream), "kf_ep_plan_p2p")
             pe.barrier(stream)                  # every rank's count row has landed here
             meta = pe.meta.cpu()                # the step's one host synchronisation
-            if int(meta[world * world]) != 0:
-                raise RuntimeError(f"peer exchange: device status {int(meta[world * world]):#x} "
-                                   "(a rank did not reach a barrier, or a receive area overflowed)")
+            err = peer_status_error(int(meta[world * world]))
+            if err:
+                raise RuntimeError(err)
             return meta[:world * world].view(world, world)
 
         counts = plan(self._peer)

@@ -102,3 +102,23 @@ def test_peer_capacity_needs():
     counts = torch.tensor([[5, 0, 7], [1, 2, 3], [0, 9, 0]], dtype=torch.int32)   # [source, destination]
     assert peer_capacity_needs(counts) == (11, 12)   # column 1: 0+2+9, row 0: 5+0+7
     assert peer_capacity_needs(torch.zeros(2, 2, dtype=torch.int32)) == (0, 0)
+
+
+def test_peer_status_errors_are_decoded_and_sticky():
+    """A non-zero status word of the peer exchange raises on check(), naming its cause, every time."""
+    from types import SimpleNamespace
+    assert ep.peer_status_error(0) is None
+    assert "barrier" in ep.peer_status_error(ep.STATUS_TIMEOUT_PEER)
+    assert "overflowed" in ep.peer_status_error(ep.STATUS_SLOT_OVERFLOW)
+    m = object.__new__(ep.ExpertParallelMoE)
+    m.plumbing = "p2p"
+    m._peer = None
+    m.check()                                           # before the first step: nothing to check
+    m._peer = SimpleNamespace(status=torch.zeros(1, dtype=torch.int32))
+    m.check()
+    m._peer.status[0] = ep.STATUS_TIMEOUT_PEER
+    for _ in range(2):
+        with pytest.raises(RuntimeError, match="0x20"):
+            m.check()
+    m.plumbing = "cuda"
+    m.check()                                           # NCCL plumbing: its collectives raise instead
