@@ -93,6 +93,14 @@ def library():
     return _load()
 
 
+def _call(device: torch.device, fn, *args) -> int:
+    """One C-ABI call with ``device`` current: the library launches on, and sets
+    itself up for, the current CUDA device, while the tensors of a call may live
+    on any device (as with the reference's operator)."""
+    with torch.cuda.device(device):
+        return fn(*args)
+
+
 def _check(rc: int, what: str) -> None:
     if rc != KF_OK:
         msg = _load().kf_moe_error_string(rc).decode()
@@ -115,6 +123,15 @@ def workspace(num_tokens: int, num_local: int, device: torch.device, stream: Opt
             buf = torch.empty(need, dtype=torch.uint8, device=device)
             _workspaces[key] = buf
     return buf
+
+
+def release_workspaces() -> None:
+    """Drop the cached scratch buffers of every device and stream (they return to
+    torch's caching allocator); the next call allocates again.  Call it only when
+    no library work is pending on those streams."""
+    with _ws_lock:
+        _workspaces.clear()
+        _ep_ws.clear()
 
 
 def _ptr(t: Optional[torch.Tensor]):
@@ -182,7 +199,7 @@ def kernel(routing_logits, routing_bias, hidden_states, hidden_states_scale, gem
         return out
     stream = torch.cuda.current_stream(device)
     ws = workspace(T, E, device, stream)
-    rc = _load().kf_moe_forward(_ptr(logits), _ptr(bias), _ptr(hid), _ptr(hs), _ptr(w13), _ptr(w13s), _ptr(w2),
+    rc = _call(device, _load().kf_moe_forward, _ptr(logits), _ptr(bias), _ptr(hid), _ptr(hs), _ptr(w13), _ptr(w13s), _ptr(w2),
                                 _ptr(w2s), T, E, offset, ctypes.c_float(rsf), _ptr(out), _ptr(ws),
                                 ctypes.c_size_t(ws.numel()), ctypes.c_void_p(stream.cuda_stream))
     _check(rc, "kf_moe_forward")
@@ -199,7 +216,7 @@ def route(routing_logits, routing_bias, routed_scaling_factor):
     w = torch.empty((T, TOP_K), dtype=torch.float32, device=device)
     if T:
         stream = torch.cuda.current_stream(device)
-        rc = _load().kf_moe_route(_ptr(logits), _ptr(bias), T, ctypes.c_float(_scalar_float(routed_scaling_factor)),
+        rc = _call(device, _load().kf_moe_route, _ptr(logits), _ptr(bias), T, ctypes.c_float(_scalar_float(routed_scaling_factor)),
                                   _ptr(idx), _ptr(w), ctypes.c_void_p(stream.cuda_stream))
         _check(rc, "kf_moe_route")
     return idx, w
@@ -227,7 +244,7 @@ def experts(topk_idx, topk_weight, hidden_states, hidden_states_scale, gemm1_wei
         return out
     stream = torch.cuda.current_stream(device)
     ws = workspace(T, E, device, stream)
-    rc = _load().kf_moe_experts(_ptr(idx), _ptr(w), _ptr(hid), _ptr(hs), _ptr(w13), _ptr(w13s), _ptr(w2), _ptr(w2s),
+    rc = _call(device, _load().kf_moe_experts, _ptr(idx), _ptr(w), _ptr(hid), _ptr(hs), _ptr(w13), _ptr(w13s), _ptr(w2), _ptr(w2s),
                                 T, E, offset, _ptr(out), 1 if out_dtype == torch.float32 else 0, _ptr(ws),
                                 ctypes.c_size_t(ws.numel()), ctypes.c_void_p(stream.cuda_stream))
     _check(rc, "kf_moe_experts")
@@ -242,7 +259,7 @@ def read_status(device: Optional[torch.device] = None) -> int:
     if buf is None:
         return 0
     st = ctypes.c_int32(0)
-    rc = _load().kf_moe_read_status(_ptr(buf), ctypes.byref(st), ctypes.c_void_p(stream.cuda_stream))
+    rc = _call(device, _load().kf_moe_read_status, _ptr(buf), ctypes.byref(st), ctypes.c_void_p(stream.cuda_stream))
     if rc not in (KF_OK, KF_ERR_DEVICE_STATUS):
         _check(rc, "kf_moe_read_status")
     return int(st.value)
@@ -283,7 +300,7 @@ def experts_packed(rows, gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm
         return out
     stream = torch.cuda.current_stream(device)
     ws = workspace(R, E, device, stream)
-    rc = _load().kf_moe_experts_packed(_ptr(rows), _ptr(w13), _ptr(w13s), _ptr(w2), _ptr(w2s), R, E,
+    rc = _call(device, _load().kf_moe_experts_packed, _ptr(rows), _ptr(w13), _ptr(w13s), _ptr(w2), _ptr(w2s), R, E,
                                        _scalar_int(local_expert_offset), _ptr(out),
                                        1 if out_dtype == torch.float32 else 0, _ptr(ws), ctypes.c_size_t(ws.numel()),
                                        ctypes.c_void_p(stream.cuda_stream))
@@ -308,7 +325,7 @@ def experts_packed_p2p(rows, gemm1_weights, gemm1_weights_scale, gemm2_weights, 
     E, w13, w13s, w2, w2s = _weights(gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, device)
     stream = torch.cuda.current_stream(device)
     ws = workspace(R, E, device, stream)
-    rc = _load().kf_moe_experts_packed_p2p(_ptr(rows), _ptr(w13), _ptr(w13s), _ptr(w2), _ptr(w2s), R, E,
+    rc = _call(device, _load().kf_moe_experts_packed_p2p, _ptr(rows), _ptr(w13), _ptr(w13s), _ptr(w2), _ptr(w2s), R, E,
                                            _scalar_int(local_expert_offset), _ptr(counts), int(rank), int(world),
                                            _ptr(peer_back), _ptr(ws), ctypes.c_size_t(ws.numel()),
                                            ctypes.c_void_p(stream.cuda_stream))
@@ -348,7 +365,7 @@ def ep_dispatch(topk_idx, topk_weight, hidden_states, hidden_states_scale, world
     if buf is None or buf.numel() < need:
         buf = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
         _ep_ws[key] = buf
-    rc = lib.kf_ep_dispatch(_ptr(idx), _ptr(w), _ptr(hid), _ptr(hs), T, int(world), _ptr(send), _ptr(counts),
+    rc = _call(device, lib.kf_ep_dispatch, _ptr(idx), _ptr(w), _ptr(hid), _ptr(hs), T, int(world), _ptr(send), _ptr(counts),
                             _ptr(pos), _ptr(buf), ctypes.c_size_t(buf.numel()), ctypes.c_void_p(stream.cuda_stream))
     _check(rc, "kf_ep_dispatch")
     return send, counts, pos
@@ -366,7 +383,7 @@ def ep_combine(partials, pos, world: int):
     partials = partials.contiguous()
     pos = pos.to(torch.int32).contiguous()
     stream = torch.cuda.current_stream(device)
-    rc = _load().kf_ep_combine(_ptr(partials) if partials.numel() else ctypes.c_void_p(0),
+    rc = _call(device, _load().kf_ep_combine, _ptr(partials) if partials.numel() else ctypes.c_void_p(0),
                                1 if partials.dtype == torch.float32 else 0, _ptr(pos), T, int(world), _ptr(out),
                                ctypes.c_void_p(stream.cuda_stream))
     _check(rc, "kf_ep_combine")
@@ -386,6 +403,6 @@ def quantize_hidden(x: torch.Tensor):
     T = x.shape[0]
     q = torch.empty((T, H), dtype=torch.float8_e4m3fn, device=x.device)
     s = torch.empty((H // 128, T), dtype=torch.float32, device=x.device)
-    rc = _load().kf_quantize_hidden(_ptr(x), T, _ptr(q), _ptr(s), torch.cuda.current_stream(x.device).cuda_stream)
+    rc = _call(x.device, _load().kf_quantize_hidden, _ptr(x), T, _ptr(q), _ptr(s), torch.cuda.current_stream(x.device).cuda_stream)
     _check(rc, "kf_quantize_hidden")
     return q, s

@@ -262,14 +262,16 @@ class ExpertParallelMoE:
         if hidden_states_scale is None and self.plumbing != "p2p":
             from . import binding as B
             hidden_states, hidden_states_scale = B.quantize_hidden(hidden_states)
-        if self.plumbing == "p2p":
-            return self._forward_p2p(routing_logits, routing_bias, hidden_states, hidden_states_scale,
-                                     routed_scaling_factor)
-        if self.plumbing == "cuda":
+        if self.plumbing == "torch":
+            return self._forward_torch(routing_logits, routing_bias, hidden_states, hidden_states_scale,
+                                       routed_scaling_factor)
+        # the library's entry points launch on the current device: make it the rows' device
+        with torch.cuda.device(hidden_states.device):
+            if self.plumbing == "p2p":
+                return self._forward_p2p(routing_logits, routing_bias, hidden_states, hidden_states_scale,
+                                         routed_scaling_factor)
             return self._forward_cuda(routing_logits, routing_bias, hidden_states, hidden_states_scale,
                                       routed_scaling_factor)
-        return self._forward_torch(routing_logits, routing_bias, hidden_states, hidden_states_scale,
-                                   routed_scaling_factor)
 
     def _forward_cuda(self, routing_logits, routing_bias, hidden_states, hidden_states_scale, routed_scaling_factor):
         from . import binding as B

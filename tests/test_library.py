@@ -67,6 +67,45 @@ def test_token_ceiling():
     assert lib.kf_quantize_hidden(null, cap + 1, null, null, null) == 1
 
 
+def test_library_calls_run_with_the_tensors_device_current(monkeypatch):
+    """_call makes the given device current around the C-ABI call (the library launches on the current device)."""
+    seen = []
+
+    class Guard:
+        def __init__(self, d):
+            self.d = d
+
+        def __enter__(self):
+            seen.append(("enter", self.d))
+
+        def __exit__(self, *exc):
+            seen.append(("exit", self.d))
+
+    monkeypatch.setattr(torch.cuda, "device", Guard)
+    dev = torch.device("cuda", 3)
+    assert B._call(dev, lambda a, b: (seen.append("call"), a + b)[1], 1, 2) == 3
+    assert seen == [("enter", dev), "call", ("exit", dev)]
+
+
+def test_every_device_entry_point_goes_through_the_device_guard():
+    """In the binding, each call of a launching entry point is made through _call."""
+    src = open(os.path.join(ROOT, "kernelforge_b200", "binding.py")).read()
+    host_only = {"kf_moe_workspace_bytes", "kf_ep_workspace_bytes", "kf_ep_max_send_rows", "kf_moe_error_string",
+                 "kf_moe_profile_begin", "kf_moe_profile_end", "kf_moe_launches_per_forward"}
+    direct = [n for n in re.findall(r"(?:_load\(\)|lib)\.(kf_\w+)\(", src) if n not in host_only]
+    assert not direct, f"called without _call: {direct}"
+    routed = re.findall(r"_call\(\s*[\w.]+,\s*(?:_load\(\)|lib)\.(kf_\w+),", src)
+    assert {"kf_moe_forward", "kf_moe_route", "kf_moe_experts", "kf_moe_experts_packed", "kf_moe_experts_packed_p2p",
+            "kf_ep_dispatch", "kf_ep_combine", "kf_quantize_hidden", "kf_moe_read_status"} <= set(routed)
+
+
+def test_release_workspaces_empties_the_caches():
+    B._workspaces[(0, 0)] = torch.empty(8, dtype=torch.uint8)
+    B._ep_ws[(0, 0)] = torch.empty(8, dtype=torch.uint8)
+    B.release_workspaces()
+    assert not B._workspaces and not B._ep_ws
+
+
 def test_error_strings():
     lib = B.library()
     assert lib.kf_moe_error_string(0) == b"ok"
