@@ -183,7 +183,8 @@ def run_reference(args, world, rank):
     if rank != 0:
         return
     T, E, name = workload_shape(args, 1)
-    cores = torch.get_num_threads() if False else (os.cpu_count() or 1)
+    torch.set_num_threads(os.cpu_count() or 1)      # every host thread, as the oracle timing below uses
+    cores = torch.get_num_threads()
     for _ in range(args.warmup):
         cpu_oracle_tokens_per_s(1, seed=7)
     times = []
@@ -209,12 +210,12 @@ def run_reference(args, world, rank):
 # ------------------------------------------------------------------- our arm --
 def main():
     args = parse()
-    world, rank, local = dist_setup(args)
     if args.impl == "reference":
-        run_reference(args, world, rank)
-        if world > 1:
-            torch.distributed.destroy_process_group()
+        # the reference's CPU path runs on rank 0 alone; under torchrun the other ranks exit
+        # at once, so this arm needs no process group (and no GPU)
+        run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))
         return
+    world, rank, local = dist_setup(args)
 
     from kernelforge_b200 import binding as B
     from kernelforge_b200 import synthetic as S
