@@ -28,6 +28,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -76,54 +77,136 @@ def load_peaks():
     return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
 
 
-class ClockSampler:
-    """nvidia-smi samples (every 200 ms) of the SM clock and throttle reasons during the timed region."""
+CLOCK_FIELDS = ("index,uuid,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                "clocks_event_reasons.sw_power_cap")
+REASON_NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.samples = []
-        self._proc = None
-        self._thread = None
 
-    def start(self):
-        cmd = ["nvidia-smi", "-i", str(self.gpu),
-               "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-               "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "200"]
+def _hex(s) -> str:
+    return re.sub(r"[^0-9a-f]", "", str(s).lower())
+
+
+def gpu_identity(dev_index: int) -> dict:
+    """How to find this CUDA device among nvidia-smi's rows: its UUID, PCI address and, as a last resort,
+    the physical index CUDA_VISIBLE_DEVICES maps it to."""
+    p = torch.cuda.get_device_properties(dev_index)
+    vis = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    phys = dev_index
+    if dev_index < len(vis) and vis[dev_index].isdigit():
+        phys = int(vis[dev_index])
+    pci = tuple(getattr(p, k, None) for k in ("pci_domain_id", "pci_bus_id", "pci_device_id"))
+    return {"uuid": _hex(getattr(p, "uuid", "")), "pci": pci if None not in pci else None, "index": phys}
+
+
+def _pci_of(field: str):
+    """(domain, bus, device) of an nvidia-smi pci.bus_id such as 00000000:17:00.0, or None."""
+    m = re.fullmatch(r"\s*([0-9a-fA-F]+):([0-9a-fA-F]+):([0-9a-fA-F]+)\.[0-9a-fA-F]+\s*", field)
+    return tuple(int(x, 16) for x in m.groups()) if m else None
+
+
+def select_gpu_rows(samples, ident):
+    """The samples of this GPU: matched by UUID, else by PCI address, else by physical index.
+    Returns (rows, how) with rows = [(time, fields)] and fields = the CLOCK_FIELDS values."""
+    if ident.get("uuid"):
+        rows = [(t, f) for t, f in samples if _hex(f[1]) == ident["uuid"]]
+        if rows:
+            return rows, "uuid"
+    if ident.get("pci"):
+        rows = [(t, f) for t, f in samples if _pci_of(f[2]) == tuple(ident["pci"])]
+        if rows:
+            return rows, "pci"
+    rows = [(t, f) for t, f in samples if f[0].strip() == str(ident.get("index"))]
+    return rows, "index"
+
+
+def summarize_clocks(rows, windows):
+    """Median SM clock, max clock and the throttle reasons seen in the first window of `windows` that
+    holds at least 3 samples (else the last, widest one).  Samples outside the windows (idle time
+    before and after the timed steps) never count."""
+    def num(x):
         try:
-            self._proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self._proc = None
-            return
-        self._thread = threading.Thread(target=self._read, daemon=True)
-        self._thread.start()
+            return float(x)
+        except ValueError:
+            return None
+    win, label = [], "none"
+    for lo, hi, name in windows:
+        win = [f for t, f in rows if lo <= t <= hi]
+        label = name
+        if len(win) >= 3:
+            break
+    if not win:
+        return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0, "window": label}
+    mhz = [v for v in (num(f[3]) for f in win) if v is not None]
+    mx = [v for v in (num(f[4]) for f in win) if v is not None]
+    reasons = sorted({REASON_NAMES[i] for f in win for i in range(4) if f[6 + i].strip().lower() == "active"})
+    return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": max(mx) if mx else None,
+            "reasons": reasons, "samples": len(win), "window": label}
 
-    def _read(self):
-        for line in self._proc.stdout:
+
+class ClockSampler:
+    """nvidia-smi samples (every 25 ms, all GPUs; this GPU's rows picked by UUID / PCI address) of the
+    SM clock and throttle reasons while the timed steps run.  If nvidia-smi ends without a sample (an
+    interval it refuses), it is started again at 200 ms."""
+
+    def __init__(self, dev_index=None, ident=None, exe: str = "nvidia-smi"):
+        self.ident = ident if ident is not None else gpu_identity(dev_index)
+        self.exe = exe
+        self.samples = []
+        self._lock = threading.Lock()
+        self._stopping = False
+        self._periods = []
+        self._proc = None
+        self._threads = []
+
+    def start(self, period_ms: int = 25):
+        self._periods = [period_ms] + ([200] if period_ms != 200 else [])
+        self._launch()
+
+    def _launch(self):
+        with self._lock:
+            if self._stopping or not self._periods:
+                return
+            cmd = [self.exe, f"--query-gpu={CLOCK_FIELDS}", "--format=csv,noheader,nounits", "-lms",
+                   str(self._periods.pop(0))]
+            try:
+                proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            except OSError:
+                return
+            self._proc = proc
+            th = threading.Thread(target=self._read, args=(proc,), daemon=True)
+            self._threads.append(th)
+            th.start()
+
+    def _read(self, proc):
+        got = 0
+        for line in proc.stdout:
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) >= 7:
+            if len(parts) >= 10:
                 self.samples.append((time.time(), parts))
+                got += 1
+        proc.wait()
+        if got == 0:
+            self._launch()
 
     def stop(self):
-        if self._proc is not None:
-            self._proc.terminate()
+        with self._lock:
+            self._stopping = True
+            proc = self._proc
+        if proc is not None and proc.poll() is None:
+            proc.terminate()
             try:
-                self._proc.wait(timeout=5)
+                proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
-                self._proc.kill()
-        if self._thread is not None:
-            self._thread.join(timeout=5)
+                proc.kill()
+        for th in list(self._threads):
+            th.join(timeout=5)
 
-    def summary(self, t0: float, t1: float):
-        window = [p for (t, p) in self.samples if t0 <= t <= t1] or [p for (_, p) in self.samples]
-        if not window:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        mhz = [float(p[0]) for p in window if p[0].replace(".", "").isdigit()]
-        mx = [float(p[1]) for p in window if p[1].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for p in window for i in range(4) if p[3 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(window)}
+    def summary(self, windows):
+        rows, how = select_gpu_rows(list(self.samples), self.ident)
+        out = summarize_clocks(rows, windows)
+        out["gpu_matched_by"] = how
+        return out
 
 
 def dist_setup(args):
@@ -262,8 +345,9 @@ def main():
         step(ti.routing_logits, ti.routing_bias, ti.hidden_states, ti.hidden_states_scale)
     torch.cuda.synchronize(dev)
 
-    clocks = ClockSampler(dev.index if world == 1 else local)
-    clocks.start()
+    clocks = ClockSampler(dev.index)
+    if rank == 0:           # only rank 0's line reports clocks; one sampler keeps the host quiet
+        clocks.start()
     time.sleep(0.5)
     stream = torch.cuda.current_stream(dev)
 
@@ -292,6 +376,7 @@ def main():
     t_wall1 = time.time()
     # the same K steps again with every library launch bracketed by CUDA events (kernel durations)
     _, _, prof = timed(args.steps, True)
+    t_wall2 = time.time()
     clocks.stop()
     if world > 1:
         t = torch.tensor([ms], device=dev)
@@ -434,7 +519,8 @@ def main():
             "active_local_experts": active,
             "roofline": roofline, "kernels": kernels, "gpu_launches": total_launches,
             "e2e": e2e, "cpu_baseline": cpu,
-            "clocks": clocks.summary(t_wall0, t_wall1),
+            "clocks": clocks.summary([(t_wall0, t_wall1, "timed steps"),
+                                      (t_wall0, t_wall2, "timed steps + the same steps profiled")]),
         }
         print(json.dumps(line), flush=True)
     if world > 1:
