@@ -67,3 +67,30 @@ def test_oracle_quantizer_matches_reference_bit_exact():
     assert torch.equal(s, s_ref)
     assert torch.equal(s[:, 6], torch.ones(56))       # all-zero row: scale 1, codes 0
     assert int(q[6].view(torch.uint8).max()) == 0
+
+
+def test_oracle_agrees_with_the_flashinfer_trace_reference():
+    """Cross-check against a second, independent statement of the same definition: flashinfer's
+    DS-routing FP8 block-scale MoE trace reference (flashinfer-python 0.6.11.post2,
+    ``flashinfer/trace/templates/moe.py``, ``_trtllm_fp8_block_scale_moe_ds_routing_reference``),
+    run on 4 local experts placed where the most tokens route (it dequantises every local expert)."""
+    fi = pytest.importorskip("flashinfer.trace.templates.moe")
+    from kernelforge_b200 import synthetic as S
+    T, E, rsf = 64, 4, 2.5
+    ti = S.token_inputs(T, seed=11)
+    idx, _ = O.route(ti.routing_logits, ti.routing_bias, rsf)
+    hist = torch.bincount(idx.flatten().long(), minlength=256)
+    offset = int(torch.stack([hist[o:o + E].sum() for o in range(256 - E + 1)]).argmax())
+    assert int(hist[offset:offset + E].sum()) >= 8            # enough pairs reach the local experts
+    wb = S.expert_bank(E, offset, seed=3)
+    ours = O.moe_layer(ti.routing_logits, ti.routing_bias, ti.hidden_states, ti.hidden_states_scale,
+                       wb.gemm1_weights, wb.gemm1_weights_scale, wb.gemm2_weights, wb.gemm2_weights_scale,
+                       offset, rsf)
+    ref = fi._trtllm_fp8_block_scale_moe_ds_routing_reference(
+        ti.routing_logits, ti.routing_bias, ti.hidden_states, ti.hidden_states_scale, wb.gemm1_weights,
+        wb.gemm1_weights_scale, wb.gemm2_weights, wb.gemm2_weights_scale, 8, 8, 4, offset, rsf)
+    assert ref.abs().max() > 0
+    assert O.check_tolerance(ours, ref)["ok"]
+    # both are fp32 restatements (different op order): far tighter than the layer's tolerance
+    d = (ours.float() - ref.float()).abs().max()
+    assert d <= 2e-3 * ref.float().abs().max(), float(d)
