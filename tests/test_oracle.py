@@ -94,3 +94,23 @@ def test_oracle_agrees_with_the_flashinfer_trace_reference():
     # both are fp32 restatements (different op order): far tighter than the layer's tolerance
     d = (ours.float() - ref.float()).abs().max()
     assert d <= 2e-3 * ref.float().abs().max(), float(d)
+
+
+@pytest.mark.parametrize("mistake", ["gate_up_swapped", "w2_scale_grid_misread"])
+def test_goldens_reject_a_wrong_weight_layout(mistake):
+    """Negative controls for the layout conventions: W13 rows are [up (X1); gate (X2)] (reference
+    ``kernel.py:1940-1943``) and the W2 scale grid is [E, H/128, I/128] (``kernel.py:118-123``).  The
+    same layer computed with either convention broken misses the reference's golden output by far
+    more than the tolerance, so the golden match above pins both conventions."""
+    case = LAYER["t16_off0"]
+    ti, wb, offset, rsf = layer_inputs(case)
+    w13, w13s, w2, w2s = wb.gemm1_weights, wb.gemm1_weights_scale, wb.gemm2_weights, wb.gemm2_weights_scale
+    if mistake == "gate_up_swapped":
+        w13 = torch.cat([w13[:, 2048:], w13[:, :2048]], dim=1)
+        w13s = torch.cat([w13s[:, 16:], w13s[:, :16]], dim=1)
+    else:   # the same 896 numbers per expert read as an [I/128, H/128] grid, then transposed into place
+        w2s = w2s.reshape(w2s.shape[0], 16, 56).transpose(1, 2).contiguous()
+    out = O.moe_layer(ti.routing_logits, ti.routing_bias, ti.hidden_states, ti.hidden_states_scale,
+                      w13, w13s, w2, w2s, offset, rsf)
+    ref = torch.from_numpy(case["out_bf16"]).view(torch.bfloat16)
+    assert not O.check_tolerance(out, ref)["ok"]
