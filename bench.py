@@ -20,8 +20,9 @@ generated on the GPU); the weights (11.3 GB) are far larger than L2, so every
 step streams them from HBM (no L2 flush needed).
 
 --impl reference times the reference algorithm's CPU path (the oracle port of
-solution/triton/kernel.py::kernel's PyTorch loop) on this host's cores, one
-bounded sample (one token) per step.
+solution/triton/kernel.py::kernel's PyTorch loop) on this host's cores: per step,
+all tokens routed and the expert loop run on 8 of the active experts, scaled to
+all of them (CpuOracleSample).
 """
 from __future__ import annotations
 
@@ -234,57 +235,93 @@ def workload_shape(args, world):
 
 
 # ---------------------------------------------------------------- CPU baseline --
-def cpu_oracle_tokens_per_s(tokens: int, seed: int = 0):
-    """The oracle (reference algorithm, PyTorch CPU) on `tokens` tokens of the workload.
+class CpuOracleSample:
+    """A bounded sample of the workload for the reference algorithm's CPU path, timed so that it
+    scales to the whole layer.
 
-    Only the experts those tokens reach are materialised (in a compact bank); the
-    timed part is the reference's own work: routing, per-expert dequantisation,
-    fp32 GEMMs, SwiGLU and the weighted index_add combine.
+    The reference's CPU layer (``solution/triton/kernel.py:1927-1950``, restated in
+    ``oracle/moe_oracle.py``) loops over the active local experts independently: each iteration
+    dequantises one expert's weights and its rows and runs that expert's two GEMMs, so dequantising
+    weights is paid once per expert and amortised over its pairs.  A sample of a few tokens would
+    pay it for a handful of pairs and understate the path's throughput by orders of magnitude.
+    This sample keeps the workload's amortisation.  It routes all T tokens, then runs the loop for
+    k of the active experts (evenly spaced) with all of their pairs, and scales that loop time by
+    active/k.  The per-call fixed work (zeroing the fp32 accumulator, the bf16 cast) is timed as a
+    call with no local pair and counted once.  The expert weights are generated once, outside the
+    timing.
     """
-    from kernelforge_b200 import synthetic as S
-    from oracle import moe_oracle as O
-    torch.set_num_threads(os.cpu_count() or 1)
-    ti = S.token_inputs(tokens, seed=seed + 1000)
-    idx, _ = O.route(ti.routing_logits, ti.routing_bias, 2.5)
-    active = sorted(set(idx.flatten().tolist()))
-    banks = [S.expert_weights(g, seed=0) for g in active]
-    w13 = torch.stack([b[0] for b in banks]); w13s = torch.stack([b[1] for b in banks])
-    w2 = torch.stack([b[2] for b in banks]); w2s = torch.stack([b[3] for b in banks])
-    lut = torch.full((E_GLOBAL,), -1, dtype=torch.int64)
-    lut[torch.tensor(active)] = torch.arange(len(active))
-    t0 = time.perf_counter()
-    idx, w = O.route(ti.routing_logits, ti.routing_bias, 2.5)
-    cidx = lut[idx]
-    wsel = torch.gather(w, 1, idx)
-    out = O.moe_experts(cidx, wsel, ti.hidden_states, ti.hidden_states_scale, w13, w13s, w2, w2s, 0)
-    out = out.to(torch.bfloat16)
-    dt = time.perf_counter() - t0
-    return tokens / dt, dt, len(active)
+
+    def __init__(self, T: int, num_local: int, offset: int = 0, k: int = 8, seed: int = 1000):
+        from kernelforge_b200 import synthetic as S
+        from oracle import moe_oracle as O
+        torch.set_num_threads(os.cpu_count() or 1)
+        self.O, self.T = O, T
+        self.ti = S.token_inputs(T, seed=seed)
+        idx, _ = O.route(self.ti.routing_logits, self.ti.routing_bias, 2.5)
+        counts = torch.bincount(idx.flatten().long(), minlength=E_GLOBAL)
+        self.active = [e for e in range(offset, offset + num_local) if counts[e] > 0]
+        # experts at the midpoints of k equal quantiles of the pair counts: the sample's pairs per
+        # expert track the population's, so both the per-expert and the per-pair work scale by active/k
+        by_count = sorted(self.active, key=lambda e: (int(counts[e]), e))
+        k = min(k, len(self.active))
+        self.sample = sorted(by_count[int((i + 0.5) * len(by_count) / k)] for i in range(k))
+        self.total_pairs = int(sum(int(counts[e]) for e in self.active))
+        banks = [S.expert_weights(g, seed=0) for g in self.sample]
+        if banks:
+            self.w = [torch.stack([b[i] for b in banks]) for i in range(4)]
+        else:
+            self.w = [t[:1] for t in (torch.zeros(1, 2 * I, H, dtype=torch.float8_e4m3fn),
+                                      torch.ones(1, 2 * I // 128, H // 128), torch.zeros(1, H, I, dtype=torch.float8_e4m3fn),
+                                      torch.ones(1, H // 128, I // 128))]
+        self.lut = torch.full((E_GLOBAL,), -1, dtype=torch.int64)
+        if self.sample:
+            self.lut[torch.tensor(self.sample)] = torch.arange(len(self.sample))
+        self.pairs = int((self.lut[idx] >= 0).sum())
+
+    def time_once(self) -> float:
+        """Estimated seconds of the whole layer on this host (one timed sample)."""
+        O, ti = self.O, self.ti
+        t0 = time.perf_counter()
+        idx, w = O.route(ti.routing_logits, ti.routing_bias, 2.5)
+        cidx = self.lut[idx]
+        wsel = torch.gather(w, 1, idx)
+        t1 = time.perf_counter()
+        O.moe_experts(cidx, wsel, ti.hidden_states, ti.hidden_states_scale, *self.w, 0).to(torch.bfloat16)
+        t2 = time.perf_counter()
+        O.moe_experts(torch.full_like(cidx, -1), wsel, ti.hidden_states, ti.hidden_states_scale, *self.w,
+                      0).to(torch.bfloat16)
+        t3 = time.perf_counter()
+        fixed = t3 - t2
+        loop = max(0.0, (t2 - t1) - fixed)
+        scale = len(self.active) / len(self.sample) if self.sample else 0.0
+        return (t1 - t0) + fixed + loop * scale
+
+    def describe(self, est_s: float) -> str:
+        return (f"all {self.T} tokens routed; the expert loop timed on {len(self.sample)} of the "
+                f"{len(self.active)} active experts ({self.pairs} of {self.total_pairs} pairs) and scaled by "
+                f"{len(self.active)}/{max(1, len(self.sample))}; estimated layer {est_s:.1f} s (PyTorch CPU, "
+                f"reference algorithm restated in oracle/moe_oracle.py)")
 
 
 def run_reference(args, world, rank):
     if rank != 0:
         return
     T, E, name = workload_shape(args, 1)
-    torch.set_num_threads(os.cpu_count() or 1)      # every host thread, as the oracle timing below uses
+    smp = CpuOracleSample(T, E)
     cores = torch.get_num_threads()
     for _ in range(args.warmup):
-        cpu_oracle_tokens_per_s(1, seed=7)
-    times = []
-    t_all = 0.0
-    for k in range(args.steps):
-        _, dt, _ = cpu_oracle_tokens_per_s(1, seed=100 + k)
-        times.append(dt)
-        t_all += dt
-    value = args.steps / t_all
+        smp.time_once()
+    ests = [smp.time_once() for _ in range(args.steps)]
+    t_all = sum(ests)
+    value = T * args.steps / t_all
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t_all / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": name, "tokens_per_gpu": T, "experts": E_GLOBAL, "sample": "1 token per step"},
+        "config": {"workload": name, "tokens_per_gpu": T, "experts": E_GLOBAL,
+                   "sample": "per step: " + smp.describe(statistics.median(ests))},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": "1 token of the workload per step through its 8 experts (PyTorch CPU, "
-                                   "reference algorithm restated in oracle/moe_oracle.py)"},
+                         "sample": smp.describe(statistics.median(ests))},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -497,10 +534,11 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        tps, dt, nact = cpu_oracle_tokens_per_s(8, seed=0)
-        cpu = {"value": tps, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-               "sample": f"8 tokens of the workload through their {nact} experts (PyTorch CPU, "
-                         f"{dt:.1f} s; reference algorithm restated in oracle/moe_oracle.py)"}
+        smp = CpuOracleSample(T, E, offset)
+        smp.time_once()                                        # warm-up
+        est = statistics.median(smp.time_once() for _ in range(3))
+        cpu = {"value": T / est, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+               "sample": "median of 3: " + smp.describe(est)}
 
     if rank == 0:
         line = {
