@@ -8,8 +8,8 @@ The reference's packer (``scripts/pack_solution.py:113-204``, driven by
 (``"<relative file>::<function>"``), ``dependencies``, the optional ``binding``
 and ``destination_passing_style``, and ``sources`` is a list of
 ``{"path", "content"}`` text files.  This packer emits the same layout for the
-CUDA build: language ``"cuda"``, binding ``"torch"`` (the README's CUDA-binding
-section lists ``"tvm-ffi"`` and ``"torch"``), value-returning style
+CUDA build: language ``"cuda"``, binding ``"torch"`` (the reference's
+``README.md:404-424`` lists ``"tvm-ffi"`` and ``"torch"`` as CUDA bindings), value-returning style
 (``destination_passing_style: false``, as the reference's ``kernel`` returns
 its output), and the entry point ``kernelforge_b200/binding.py::kernel`` whose
 ten positional parameters are the reference's.
