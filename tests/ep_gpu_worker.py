@@ -55,6 +55,8 @@ def worker(rank, world, port, T, result_dir):
         res["p2p_equal_nccl"] = [bool(torch.equal(o, o_nccl)) for o in o_p2p]
         res["p2p_vs_ref"] = O.check_tolerance(o_p2p[1], ref.to(torch.bfloat16))
         res["p2p_pairs"] = p2p.local_pairs()
+        p2p.check()                                        # no barrier gave up, no receive area overflowed
+        res["p2p_status"] = p2p.status()
         res["nccl_pairs"] = nccl.local_pairs()
         # uneven token counts (one rank empty in the second step): the receive and return areas are
         # sized from the count matrix every rank holds, and grow together when a step needs more
@@ -72,6 +74,7 @@ def worker(rank, world, port, T, result_dir):
                                full.gemm1_weights_scale, full.gemm2_weights, full.gemm2_weights_scale, 0)
             res["uneven"].append(O.check_tolerance(ou, ru.to(torch.bfloat16)))
         res["uneven_caps"] = (uneven._peer.recv_cap, uneven._peer.send_cap)
+        res["uneven_status"] = uneven.status()
         dist.barrier()
         dist.destroy_process_group()
     except Exception as exc:

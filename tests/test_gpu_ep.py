@@ -42,3 +42,4 @@ def test_ep_two_gpus(tmp_path):
         assert res["p2p_vs_ref"]["ok"], res
         assert res["p2p_pairs"] == res["nccl_pairs"], res
         assert all(u["ok"] for u in res["uneven"]), res["uneven"]
+        assert res["p2p_status"] == 0 and res["uneven_status"] == 0, res
