@@ -199,9 +199,9 @@ def kernel(routing_logits, routing_bias, hidden_states, hidden_states_scale, gem
         return out
     stream = torch.cuda.current_stream(device)
     ws = workspace(T, E, device, stream)
-    rc = _call(device, _load().kf_moe_forward, _ptr(logits), _ptr(bias), _ptr(hid), _ptr(hs), _ptr(w13), _ptr(w13s), _ptr(w2),
-                                _ptr(w2s), T, E, offset, ctypes.c_float(rsf), _ptr(out), _ptr(ws),
-                                ctypes.c_size_t(ws.numel()), ctypes.c_void_p(stream.cuda_stream))
+    rc = _call(device, _load().kf_moe_forward, _ptr(logits), _ptr(bias), _ptr(hid), _ptr(hs), _ptr(w13), _ptr(w13s),
+               _ptr(w2), _ptr(w2s), T, E, offset, ctypes.c_float(rsf), _ptr(out), _ptr(ws),
+               ctypes.c_size_t(ws.numel()), ctypes.c_void_p(stream.cuda_stream))
     _check(rc, "kf_moe_forward")
     return out
 
@@ -216,8 +216,9 @@ def route(routing_logits, routing_bias, routed_scaling_factor):
     w = torch.empty((T, TOP_K), dtype=torch.float32, device=device)
     if T:
         stream = torch.cuda.current_stream(device)
-        rc = _call(device, _load().kf_moe_route, _ptr(logits), _ptr(bias), T, ctypes.c_float(_scalar_float(routed_scaling_factor)),
-                                  _ptr(idx), _ptr(w), ctypes.c_void_p(stream.cuda_stream))
+        rc = _call(device, _load().kf_moe_route, _ptr(logits), _ptr(bias), T,
+                   ctypes.c_float(_scalar_float(routed_scaling_factor)), _ptr(idx), _ptr(w),
+                   ctypes.c_void_p(stream.cuda_stream))
         _check(rc, "kf_moe_route")
     return idx, w
 
@@ -244,9 +245,9 @@ def experts(topk_idx, topk_weight, hidden_states, hidden_states_scale, gemm1_wei
         return out
     stream = torch.cuda.current_stream(device)
     ws = workspace(T, E, device, stream)
-    rc = _call(device, _load().kf_moe_experts, _ptr(idx), _ptr(w), _ptr(hid), _ptr(hs), _ptr(w13), _ptr(w13s), _ptr(w2), _ptr(w2s),
-                                T, E, offset, _ptr(out), 1 if out_dtype == torch.float32 else 0, _ptr(ws),
-                                ctypes.c_size_t(ws.numel()), ctypes.c_void_p(stream.cuda_stream))
+    rc = _call(device, _load().kf_moe_experts, _ptr(idx), _ptr(w), _ptr(hid), _ptr(hs), _ptr(w13), _ptr(w13s),
+               _ptr(w2), _ptr(w2s), T, E, offset, _ptr(out), 1 if out_dtype == torch.float32 else 0, _ptr(ws),
+               ctypes.c_size_t(ws.numel()), ctypes.c_void_p(stream.cuda_stream))
     _check(rc, "kf_moe_experts")
     return out
 
@@ -301,9 +302,8 @@ def experts_packed(rows, gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm
     stream = torch.cuda.current_stream(device)
     ws = workspace(R, E, device, stream)
     rc = _call(device, _load().kf_moe_experts_packed, _ptr(rows), _ptr(w13), _ptr(w13s), _ptr(w2), _ptr(w2s), R, E,
-                                       _scalar_int(local_expert_offset), _ptr(out),
-                                       1 if out_dtype == torch.float32 else 0, _ptr(ws), ctypes.c_size_t(ws.numel()),
-                                       ctypes.c_void_p(stream.cuda_stream))
+               _scalar_int(local_expert_offset), _ptr(out), 1 if out_dtype == torch.float32 else 0, _ptr(ws),
+               ctypes.c_size_t(ws.numel()), ctypes.c_void_p(stream.cuda_stream))
     _check(rc, "kf_moe_experts_packed")
     return out
 
@@ -325,10 +325,9 @@ def experts_packed_p2p(rows, gemm1_weights, gemm1_weights_scale, gemm2_weights, 
     E, w13, w13s, w2, w2s = _weights(gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, device)
     stream = torch.cuda.current_stream(device)
     ws = workspace(R, E, device, stream)
-    rc = _call(device, _load().kf_moe_experts_packed_p2p, _ptr(rows), _ptr(w13), _ptr(w13s), _ptr(w2), _ptr(w2s), R, E,
-                                           _scalar_int(local_expert_offset), _ptr(counts), int(rank), int(world),
-                                           _ptr(peer_back), _ptr(ws), ctypes.c_size_t(ws.numel()),
-                                           ctypes.c_void_p(stream.cuda_stream))
+    rc = _call(device, _load().kf_moe_experts_packed_p2p, _ptr(rows), _ptr(w13), _ptr(w13s), _ptr(w2), _ptr(w2s), R,
+               E, _scalar_int(local_expert_offset), _ptr(counts), int(rank), int(world), _ptr(peer_back), _ptr(ws),
+               ctypes.c_size_t(ws.numel()), ctypes.c_void_p(stream.cuda_stream))
     _check(rc, "kf_moe_experts_packed_p2p")
 
 
@@ -365,8 +364,9 @@ def ep_dispatch(topk_idx, topk_weight, hidden_states, hidden_states_scale, world
     if buf is None or buf.numel() < need:
         buf = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
         _ep_ws[key] = buf
-    rc = _call(device, lib.kf_ep_dispatch, _ptr(idx), _ptr(w), _ptr(hid), _ptr(hs), T, int(world), _ptr(send), _ptr(counts),
-                            _ptr(pos), _ptr(buf), ctypes.c_size_t(buf.numel()), ctypes.c_void_p(stream.cuda_stream))
+    rc = _call(device, lib.kf_ep_dispatch, _ptr(idx), _ptr(w), _ptr(hid), _ptr(hs), T, int(world), _ptr(send),
+               _ptr(counts), _ptr(pos), _ptr(buf), ctypes.c_size_t(buf.numel()),
+               ctypes.c_void_p(stream.cuda_stream))
     _check(rc, "kf_ep_dispatch")
     return send, counts, pos
 
@@ -384,8 +384,8 @@ def ep_combine(partials, pos, world: int):
     pos = pos.to(torch.int32).contiguous()
     stream = torch.cuda.current_stream(device)
     rc = _call(device, _load().kf_ep_combine, _ptr(partials) if partials.numel() else ctypes.c_void_p(0),
-                               1 if partials.dtype == torch.float32 else 0, _ptr(pos), T, int(world), _ptr(out),
-                               ctypes.c_void_p(stream.cuda_stream))
+               1 if partials.dtype == torch.float32 else 0, _ptr(pos), T, int(world), _ptr(out),
+               ctypes.c_void_p(stream.cuda_stream))
     _check(rc, "kf_ep_combine")
     return out
 
@@ -403,6 +403,7 @@ def quantize_hidden(x: torch.Tensor):
     T = x.shape[0]
     q = torch.empty((T, H), dtype=torch.float8_e4m3fn, device=x.device)
     s = torch.empty((H // 128, T), dtype=torch.float32, device=x.device)
-    rc = _call(x.device, _load().kf_quantize_hidden, _ptr(x), T, _ptr(q), _ptr(s), torch.cuda.current_stream(x.device).cuda_stream)
+    rc = _call(x.device, _load().kf_quantize_hidden, _ptr(x), T, _ptr(q), _ptr(s),
+               torch.cuda.current_stream(x.device).cuda_stream)
     _check(rc, "kf_quantize_hidden")
     return q, s
