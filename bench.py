@@ -245,8 +245,8 @@ class CpuOracleSample:
     weights is paid once per expert and amortised over its pairs.  A sample of a few tokens would
     pay it for a handful of pairs and understate the path's throughput by orders of magnitude.
     This sample keeps the workload's amortisation.  It routes all T tokens, then runs the loop for
-    k of the active experts (evenly spaced) with all of their pairs, and scales that loop time by
-    active/k.  The per-call fixed work (zeroing the fp32 accumulator, the bf16 cast) is timed as a
+    k of the active experts (at the midpoints of k quantiles of the per-expert pair counts) with all
+    of their pairs, and scales that loop time by active/k.  The per-call fixed work (zeroing the fp32 accumulator, the bf16 cast) is timed as a
     call with no local pair and counted once.  The expert weights are generated once, outside the
     timing.
     """
