@@ -266,13 +266,9 @@ class CpuOracleSample:
         k = min(k, len(self.active))
         self.sample = sorted(by_count[int((i + 0.5) * len(by_count) / k)] for i in range(k))
         self.total_pairs = int(sum(int(counts[e]) for e in self.active))
-        banks = [S.expert_weights(g, seed=0) for g in self.sample]
-        if banks:
-            self.w = [torch.stack([b[i] for b in banks]) for i in range(4)]
-        else:
-            self.w = [t[:1] for t in (torch.zeros(1, 2 * I, H, dtype=torch.float8_e4m3fn),
-                                      torch.ones(1, 2 * I // 128, H // 128), torch.zeros(1, H, I, dtype=torch.float8_e4m3fn),
-                                      torch.ones(1, H // 128, I // 128))]
+        # with no local pair the loop is empty and never reads the (placeholder) weights
+        banks = [S.expert_weights(g, seed=0) for g in (self.sample or [offset])]
+        self.w = [torch.stack([b[i] for b in banks]) for i in range(4)]
         self.lut = torch.full((E_GLOBAL,), -1, dtype=torch.int64)
         if self.sample:
             self.lut[torch.tensor(self.sample)] = torch.arange(len(self.sample))
