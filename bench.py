@@ -530,11 +530,19 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        smp = CpuOracleSample(T, E, offset)
-        smp.time_once()                                        # warm-up
-        est = statistics.median(smp.time_once() for _ in range(3))
-        cpu = {"value": T / est, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
-               "sample": "median of 3: " + smp.describe(est)}
+        try:        # a failure here must not cost the measured line above it
+            smp = CpuOracleSample(T, E, offset)
+            smp.time_once()                                    # warm-up
+            est = statistics.median(smp.time_once() for _ in range(3))
+            cpu = {"value": T / est, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+                   "sample": "median of 3: " + smp.describe(est)}
+        except Exception as exc:  # noqa: BLE001 -- reported in the line, not swallowed
+            cpu = {"value": None, "unit": "tokens/s", "error": f"{type(exc).__name__}: {exc}"}
+    try:
+        clock_summary = clocks.summary([(t_wall0, t_wall1, "timed steps"),
+                                        (t_wall0, t_wall2, "timed steps + the same steps profiled")])
+    except Exception as exc:  # noqa: BLE001
+        clock_summary = {"sm_mhz": None, "reasons": ["unsampled"], "error": f"{type(exc).__name__}: {exc}"}
 
     if rank == 0:
         line = {
@@ -553,8 +561,7 @@ def main():
             "active_local_experts": active,
             "roofline": roofline, "kernels": kernels, "gpu_launches": total_launches,
             "e2e": e2e, "cpu_baseline": cpu,
-            "clocks": clocks.summary([(t_wall0, t_wall1, "timed steps"),
-                                      (t_wall0, t_wall2, "timed steps + the same steps profiled")]),
+            "clocks": clock_summary,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
