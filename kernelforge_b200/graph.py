@@ -4,8 +4,10 @@ At decode sizes the layer's few kernels each take a few microseconds, so the
 host's launch path (Python, ctypes, argument checks, one launch per kernel)
 sets the pace.  ``GraphedMoE`` captures one ``kernel(...)`` call into a CUDA
 graph with static input and output buffers and replays it: a replay costs one
-graph launch.  The forward has no host synchronisation and allocates nothing
-after its first call, so it captures as is.
+graph launch.  The forward has no host synchronisation, so it captures as is: a
+first call outside the capture sets the library up, and what the captured call
+allocates (its output, and the workspace cached for the capture stream) comes
+from the graph's private memory pool and stays with the graph.
 
     layer = GraphedMoE(weights, local_expert_offset=0, routed_scaling_factor=2.5, num_tokens=16)
     out = layer(routing_logits, routing_bias, hidden_states, hidden_states_scale)
