@@ -46,7 +46,7 @@ class GraphedMoE:
         side = torch.cuda.Stream(self.device)
         side.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(side):
-            self._run()  # first call: device set-up and tensor maps happen outside the capture
+            self._run()  # first call: the library's one-time device set-up (kernel attributes) runs outside the capture
         torch.cuda.current_stream(self.device).wait_stream(side)
         torch.cuda.synchronize(self.device)
         g = torch.cuda.CUDAGraph()
