@@ -299,6 +299,20 @@ class CpuOracleSample:
                 f"reference algorithm restated in oracle/moe_oracle.py)")
 
 
+def measure_cpu_baseline(T: int, num_local: int, offset: int, repeats: int = 3) -> dict:
+    """The ``cpu_baseline`` object of the bench line: the median of `repeats` CpuOracleSample
+    estimates after one warm-up.  A failure is reported inside the object (it must not cost the
+    measured line it rides on)."""
+    try:
+        smp = CpuOracleSample(T, num_local, offset)
+        smp.time_once()
+        est = statistics.median(smp.time_once() for _ in range(repeats))
+        return {"value": T / est, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+                "sample": f"median of {repeats}: " + smp.describe(est)}
+    except Exception as exc:  # noqa: BLE001 -- reported in the line, not swallowed
+        return {"value": None, "unit": "tokens/s", "error": f"{type(exc).__name__}: {exc}"}
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return
@@ -530,14 +544,7 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        try:        # a failure here must not cost the measured line above it
-            smp = CpuOracleSample(T, E, offset)
-            smp.time_once()                                    # warm-up
-            est = statistics.median(smp.time_once() for _ in range(3))
-            cpu = {"value": T / est, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
-                   "sample": "median of 3: " + smp.describe(est)}
-        except Exception as exc:  # noqa: BLE001 -- reported in the line, not swallowed
-            cpu = {"value": None, "unit": "tokens/s", "error": f"{type(exc).__name__}: {exc}"}
+        cpu = measure_cpu_baseline(T, E, offset)
     try:
         clock_summary = clocks.summary([(t_wall0, t_wall1, "timed steps"),
                                         (t_wall0, t_wall2, "timed steps + the same steps profiled")])

@@ -142,3 +142,14 @@ def test_clock_sampler_without_nvidia_smi_reports_unsampled():
     cs.start()
     cs.stop()
     assert cs.summary([(0.0, 1e12, "timed steps")])["reasons"] == ["unsampled"]
+
+
+def test_cpu_baseline_object_of_the_bench_line():
+    """The main arm's cpu_baseline on a decode-sized workload (16 tokens, 32 local experts), and its
+    error report when the sample cannot be built."""
+    b = _bench()
+    c = b.measure_cpu_baseline(16, 32, 0, repeats=1)
+    assert c["kind"] == "port" and c["value"] > 0 and c["cores"] >= 1 and "active experts" in c["sample"]
+    for args in ((16, 32, 300), (-1, 32, 0)):   # experts past 256 / no inputs: reported, not raised
+        err = b.measure_cpu_baseline(*args, repeats=1)
+        assert err["value"] is None and err["error"]
