@@ -274,8 +274,8 @@ int kf_moe_read_status(void* workspace, int32_t* status, void* stream);
  * contents (each call clears the status word it needs zeroed and overwrites
  * everything else before reading it): calls that overlap on the GPU -- on
  * different streams or from different threads -- race on it and must be
- * serialised by the caller.  Device-side status bits of these calls are not
- * readable through kf_moe_read_status.
+ * serialised by the caller.  Their device-side status bits are read with
+ * kf_moe_noalloc_read_status below, not with kf_moe_read_status.
  */
 int kf_moe_forward_noalloc(const float* routing_logits, const void* routing_bias,
                            const void* hidden_states, const float* hidden_states_scale,
@@ -283,6 +283,16 @@ int kf_moe_forward_noalloc(const float* routing_logits, const void* routing_bias
                            const void* gemm2_weights, const float* gemm2_weights_scale,
                            int32_t num_tokens, int32_t num_local_experts, int32_t local_expert_offset,
                            float routed_scaling_factor, void* output, void* stream);
+
+/*
+ * Status word of kf_moe_forward_noalloc's calls on the current device, for the
+ * same callers (it has no counterpart in the reference either): synchronises
+ * `stream`, copies the word into *status (host pointer) and clears it, all
+ * without allocating.  Returns KF_ERR_DEVICE_STATUS if any bit was set (a
+ * bounded wait that gave up, or a bounds check that failed, in a call since the
+ * last read).
+ */
+int kf_moe_noalloc_read_status(int32_t* status, void* stream);
 
 /* Kernel ids for the profiling counters. */
 #define KF_KERNEL_ROUTE 0

@@ -3,7 +3,11 @@
 ``kernel`` keeps the reference's signature, argument meaning and value-returning
 style (``solution/triton/kernel.py:1817-1828``): ten positional arguments, the
 two scalars given as Python numbers or 0-d tensors, a new bf16 ``[T, 7168]``
-tensor returned on the input device.  Errors raise ``RuntimeError``.
+tensor returned on the input device.  Errors raise ``RuntimeError``.  It is a
+thin wrapper over the PyTorch C++ extension ``_kf_torch`` (``csrc/kf_torch_ext.cpp``),
+which checks the tensors and calls ``kf_moe_forward`` on the current torch
+stream; the other entry points (routing, experts, expert-parallel exchange,
+quantiser) reach the same C ABI through ``ctypes``.
 
 PyTorch is only plumbing here: it owns device memory (outputs and the cached
 workspace come from its caching allocator) and the current stream.  All compute
@@ -30,6 +34,24 @@ _lib_lock = threading.Lock()
 
 KF_OK = 0
 KF_ERR_DEVICE_STATUS = 6
+
+# Device status bits (kf_moe.h KF_STATUS_*): set by the kernels, read back by the host.
+STATUS_BITS = {
+    0x01: "a TMA producer timed out waiting for a free stage",
+    0x02: "the MMA issuer timed out waiting for data or tensor memory",
+    0x04: "a promotion/epilogue warp timed out",
+    0x08: "a routed expert id outside [0, 256)",
+    0x10: "a permuted row index beyond the workspace capacity",
+    0x20: "a peer rank did not reach a barrier in time",
+}
+
+
+def status_message(status: int) -> str:
+    """Text for a non-zero device status word."""
+    what = [v for k, v in STATUS_BITS.items() if status & k]
+    if status & ~sum(STATUS_BITS):
+        what.append("unknown bits")
+    return f"device status {status:#x}: " + "; ".join(what)
 
 
 def _load():
@@ -93,6 +115,32 @@ def library():
     return _load()
 
 
+_ext_mod = None
+
+
+def extension():
+    """The torch extension module ``_kf_torch`` (built on first use if missing); ``libkf_moe.so``
+    is loaded first, so the extension's dependency on it resolves to that copy."""
+    global _ext_mod
+    if _ext_mod is not None:
+        return _ext_mod
+    with _lib_lock:
+        if _ext_mod is None:
+            import importlib.machinery
+            import importlib.util
+
+            from . import build as _build
+            _load()
+            if not _build.ext_up_to_date():
+                _build.build_ext()
+            loader = importlib.machinery.ExtensionFileLoader("_kf_torch", _build.EXT)
+            spec = importlib.util.spec_from_file_location("_kf_torch", _build.EXT, loader=loader)
+            mod = importlib.util.module_from_spec(spec)
+            loader.exec_module(mod)
+            _ext_mod = mod
+    return _ext_mod
+
+
 def _call(device: torch.device, fn, *args) -> int:
     """One C-ABI call with ``device`` current: the library launches on, and sets
     itself up for, the current CUDA device, while the tensors of a call may live
@@ -112,17 +160,54 @@ def _check(rc: int, what: str) -> None:
 _workspaces: dict = {}
 _ws_lock = threading.Lock()
 
+# Device errors raise on the host without a synchronisation per call: after each
+# launch the workspace's status word (its first 4 bytes, written by the kernels,
+# cleared by the next call on that workspace) is copied asynchronously into a
+# pinned host word and an event is recorded.  Every later call on the workspace
+# first looks at the copies whose events have completed and raises RuntimeError
+# for a non-zero word; read_status() synchronises and reports at once.
+_pending: dict = {}      # workspace key -> [(pinned int32 [1], event)] in launch order
+_free_mirrors: list = []
+
+
+def _check_pending(key) -> None:
+    q = _pending.get(key)
+    while q and q[0][1].query():
+        mirror, ev = q.pop(0)
+        v = int(mirror[0])
+        _free_mirrors.append((mirror, ev))
+        if v:
+            raise RuntimeError("an earlier call on this stream failed on the device: " + status_message(v))
+
+
+def _mirror_status(key, buf: torch.Tensor, stream) -> None:
+    if torch.cuda.is_current_stream_capturing():
+        return        # a captured call's status is not mirrored (the graph replays without host checks)
+    mirror, ev = _free_mirrors.pop() if _free_mirrors else (torch.zeros(1, dtype=torch.int32).pin_memory(),
+                                                            torch.cuda.Event())
+    with torch.cuda.stream(stream):
+        mirror.copy_(buf[:4].view(torch.int32), non_blocking=True)
+    ev.record(stream)
+    _pending.setdefault(key, []).append((mirror, ev))
+
 
 def workspace(num_tokens: int, num_local: int, device: torch.device, stream: Optional[torch.cuda.Stream] = None):
     need = int(_load().kf_moe_workspace_bytes(int(num_tokens), int(num_local)))
     stream = stream or torch.cuda.current_stream(device)
     key = (device.index, stream.cuda_stream)
     with _ws_lock:
+        _check_pending(key)
         buf = _workspaces.get(key)
         if buf is None or buf.numel() < need:
             buf = torch.empty(need, dtype=torch.uint8, device=device)
             _workspaces[key] = buf
     return buf
+
+
+def _launched(device: torch.device, stream, buf: torch.Tensor) -> None:
+    """Bookkeeping after a successful launch on ``buf``: mirror its status word."""
+    with _ws_lock:
+        _mirror_status((device.index, stream.cuda_stream), buf, stream)
 
 
 def release_workspaces() -> None:
@@ -132,6 +217,9 @@ def release_workspaces() -> None:
     with _ws_lock:
         _workspaces.clear()
         _ep_ws.clear()
+        _pending.clear()
+    if _ext_mod is not None:
+        _ext_mod.release_workspaces()
 
 
 def _ptr(t: Optional[torch.Tensor]):
@@ -181,29 +269,11 @@ def kernel(routing_logits, routing_bias, hidden_states, hidden_states_scale, gem
     gemm2_weights_scale f32 [E,56,16]; local_expert_offset / routed_scaling_factor
     as numbers or 0-d tensors.  E (local experts) is taken from the weights.
     """
-    device = hidden_states.device
-    if device.type != "cuda":
+    if hidden_states.device.type != "cuda":
         raise RuntimeError("kernelforge_b200.kernel needs CUDA tensors on a B200 (sm_100a); no CPU fallback")
-    T = int(routing_logits.shape[0])
-    offset = _scalar_int(local_expert_offset)
-    rsf = _scalar_float(routed_scaling_factor)
-    logits = _expect(routing_logits, "routing_logits", torch.float32, (T, E_GLOBAL), device)
-    bias = _expect(routing_bias.reshape(-1), "routing_bias", torch.bfloat16, (E_GLOBAL,), device)
-    hid = _expect(hidden_states, "hidden_states", torch.float8_e4m3fn, (T, H), device)
-    hs = _expect(hidden_states_scale, "hidden_states_scale", torch.float32, (H // 128, T), device)
-    E, w13, w13s, w2, w2s = _weights(gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, device)
-    if not (0 <= offset and offset + E <= E_GLOBAL):
-        raise ValueError(f"local experts [{offset}, {offset + E}) outside [0, {E_GLOBAL})")
-    out = torch.empty((T, H), dtype=torch.bfloat16, device=device)
-    if T == 0:
-        return out
-    stream = torch.cuda.current_stream(device)
-    ws = workspace(T, E, device, stream)
-    rc = _call(device, _load().kf_moe_forward, _ptr(logits), _ptr(bias), _ptr(hid), _ptr(hs), _ptr(w13), _ptr(w13s),
-               _ptr(w2), _ptr(w2s), T, E, offset, ctypes.c_float(rsf), _ptr(out), _ptr(ws),
-               ctypes.c_size_t(ws.numel()), ctypes.c_void_p(stream.cuda_stream))
-    _check(rc, "kf_moe_forward")
-    return out
+    return extension().kernel(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+                              gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
+                              _scalar_int(local_expert_offset), _scalar_float(routed_scaling_factor))
 
 
 def route(routing_logits, routing_bias, routed_scaling_factor):
@@ -249,21 +319,40 @@ def experts(topk_idx, topk_weight, hidden_states, hidden_states_scale, gemm1_wei
                _ptr(w2), _ptr(w2s), T, E, offset, _ptr(out), 1 if out_dtype == torch.float32 else 0, _ptr(ws),
                ctypes.c_size_t(ws.numel()), ctypes.c_void_p(stream.cuda_stream))
     _check(rc, "kf_moe_experts")
+    _launched(device, stream, ws)
     return out
 
 
 def read_status(device: Optional[torch.device] = None) -> int:
-    """Synchronise and return (then clear) the device status word of the current stream's workspace."""
+    """Synchronise and return (then clear) the device status word of the current stream's workspace.
+
+    Also settles the asynchronous status copies of earlier calls on that workspace, so a
+    non-zero word is reported here once rather than raised again by the next call.
+    """
     device = device or torch.device("cuda", torch.cuda.current_device())
     stream = torch.cuda.current_stream(device)
-    buf = _workspaces.get((device.index, stream.cuda_stream))
+    key = (device.index, stream.cuda_stream)
+    from_ext = int(_ext_mod.read_status(device.index)) if _ext_mod is not None else 0   # kernel() calls
+    buf = _workspaces.get(key)
     if buf is None:
-        return 0
+        return from_ext
     st = ctypes.c_int32(0)
     rc = _call(device, _load().kf_moe_read_status, _ptr(buf), ctypes.byref(st), ctypes.c_void_p(stream.cuda_stream))
     if rc not in (KF_OK, KF_ERR_DEVICE_STATUS):
         _check(rc, "kf_moe_read_status")
-    return int(st.value)
+    earlier = 0
+    with _ws_lock:
+        for mirror, ev in _pending.pop(key, []):
+            earlier |= int(mirror[0])
+            _free_mirrors.append((mirror, ev))
+    return int(st.value) | earlier | from_ext
+
+
+def check(device: Optional[torch.device] = None) -> None:
+    """Synchronise and raise ``RuntimeError`` if a call on the current stream set a device status bit."""
+    st = read_status(device)
+    if st:
+        raise RuntimeError(status_message(st))
 
 
 KERNEL_NAMES = ["route", "masks_from_topk", "permute_scan", "permute_assign", "gather_rows", "gemm1_swiglu",
@@ -305,6 +394,7 @@ def experts_packed(rows, gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm
                _scalar_int(local_expert_offset), _ptr(out), 1 if out_dtype == torch.float32 else 0, _ptr(ws),
                ctypes.c_size_t(ws.numel()), ctypes.c_void_p(stream.cuda_stream))
     _check(rc, "kf_moe_experts_packed")
+    _launched(device, stream, ws)
     return out
 
 
@@ -329,6 +419,7 @@ def experts_packed_p2p(rows, gemm1_weights, gemm1_weights_scale, gemm2_weights, 
                E, _scalar_int(local_expert_offset), _ptr(counts), int(rank), int(world), _ptr(peer_back), _ptr(ws),
                ctypes.c_size_t(ws.numel()), ctypes.c_void_p(stream.cuda_stream))
     _check(rc, "kf_moe_experts_packed_p2p")
+    _launched(device, stream, ws)
 
 
 _ep_ws: dict = {}

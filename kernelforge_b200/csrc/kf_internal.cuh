@@ -34,8 +34,7 @@ __device__ __forceinline__ float silu_f(float x) { return x * __fdividef(1.0f, 1
 struct Meta {
   int32_t num_tiles;       // row tiles of 128 permuted rows, over all local experts
   int32_t num_pairs;       // local (token, expert) pairs
-  int32_t num_ptiles;      // pair tiles of 256 rows (two CTAs of a 2-SM MMA), over all local experts
-  int32_t reserved[61];
+  int32_t reserved[62];
   int32_t expert_count[kMaxLocalExperts];      // pairs per local expert
   int32_t expert_pad_start[kMaxLocalExperts];  // first permuted row of each expert (128-aligned)
 };
@@ -43,7 +42,7 @@ struct Meta {
 // Offsets (bytes) of every scratch array inside the caller's workspace.
 struct Workspace {
   size_t status, meta, topk_idx, topk_w, token_slot, chunk_masks, chunk_base;
-  size_t tile_expert, tile_row0, tile_rows, ptile_expert, ptile_row0, ptile_rows, slot_token, slot_weight, slot_pair;
+  size_t tile_expert, tile_row0, tile_rows, slot_token, slot_weight, slot_pair;
   size_t a_rows, a_scale, c_hi, c_lo, c_scale, y, partial;
   size_t total;
   int32_t p_cap;    // capacity in permuted rows (multiple of 128)
@@ -92,11 +91,9 @@ inline RowLayout packed_layout(const void* rows) {
                    kPackedRowBytes, reinterpret_cast<const float*>(b + kH), kPackedRowBytes / 4, 1};
 }
 
-// Programmatic dependent launch for the layer's launch chain (on unless the
-// environment sets KF_MOE_PDL=0): a kernel launched this way may start while its
-// predecessor in the stream is finishing, and must begin with grid_dep_wait().
-bool pdl_enabled();
-
+// Every kernel of the layer's launch chain is launched with programmatic stream
+// serialization: it may start while its predecessor in the stream is finishing,
+// and begins with grid_dep_wait().
 template <typename... KArgs, typename... Args>
 cudaError_t launch_chained(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
                            Args&&... args) {
@@ -109,7 +106,7 @@ cudaError_t launch_chained(void (*kernel)(KArgs...), dim3 grid, dim3 block, size
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
@@ -119,8 +116,8 @@ cudaError_t launch_route(const float* logits, const void* bias, int T, float rsf
 cudaError_t launch_masks_from_topk(const RowLayout& in, int T, int E, int offset, uint4* chunk_masks, int* status,
                                    cudaStream_t s);
 cudaError_t launch_permute_scan(const uint4* chunk_masks, int nchunk, int E, Meta* meta, int32_t* chunk_base,
-                                int32_t* tile_expert, int32_t* tile_row0, int32_t* tile_rows, int32_t* ptile_expert,
-                                int32_t* ptile_row0, int32_t* ptile_rows, int nt_cap, int* status, cudaStream_t s);
+                                int32_t* tile_expert, int32_t* tile_row0, int32_t* tile_rows, int nt_cap, int* status,
+                                cudaStream_t s);
 cudaError_t launch_permute_assign(const RowLayout& in, const uint4* chunk_masks, const int32_t* chunk_base,
                                   const Meta* meta, int T, int E, int offset, int p_cap, int32_t* token_slot,
                                   int32_t* slot_token, float* slot_weight, int32_t* slot_pair, int* status,
@@ -129,8 +126,7 @@ cudaError_t launch_permute_assign(const RowLayout& in, const uint4* chunk_masks,
 // caller's routing (topk_in), tile lists, slots and the row gather.
 cudaError_t launch_front_small(const float* logits, const void* bias, float rsf, const RowLayout& in, int T, int E,
                                int offset, int p_cap, Meta* meta, int32_t* tile_expert, int32_t* tile_row0,
-                               int32_t* tile_rows, int32_t* ptile_expert, int32_t* ptile_row0, int32_t* ptile_rows,
-                               int32_t* token_slot, int32_t* slot_token, float* slot_weight, int32_t* slot_pair,
+                               int32_t* tile_rows, int32_t* token_slot, int32_t* slot_token, float* slot_weight, int32_t* slot_pair,
                                uint8_t* a_rows, float* a_scale, int* status, cudaStream_t s);
 cudaError_t launch_gather_rows(const Meta* meta, const int32_t* tile_rows, const int32_t* slot_token,
                                const RowLayout& in, int p_cap, uint8_t* a_rows, float* a_scale, int grid,
@@ -145,10 +141,8 @@ struct PeerOut {
 };
 
 cudaError_t launch_reduce(const int32_t* token_slot, const float* y, int T, void* out, int out_fp32, const PeerOut& po,
-                          cudaStream_t s);
+                          int grid, cudaStream_t s);
 
-// The tile fields hold 128-row tiles for the single-CTA kernels and 256-row pair
-// tiles for the CTA-pair kernels.
 struct Gemm1Args {
   const Meta* meta;
   const int32_t* tile_expert;
@@ -161,7 +155,7 @@ struct Gemm1Args {
   float* c_scale;          // [16][p_cap]
   int32_t p_cap;
   int* status;
-  // Split-K (single-CTA kernel only): ksplit CTAs share a (tile, column block),
+  // Split-K: ksplit CTAs share a (tile, column block),
   // each over 56/ksplit K chunks, and store their fp32 partial sums in `partial`
   // ([ksplit][max_pairs][4096], indexed by the pair id slot_pair[row]);
   // swiglu_quant_kernel then sums them in split order and runs the epilogue.
@@ -190,16 +184,8 @@ cudaError_t launch_gemm1(const CUtensorMap& tm_a, const CUtensorMap& tm_a32, con
 cudaError_t launch_gemm2(const CUtensorMap& tm_chi, const CUtensorMap& tm_clo, const CUtensorMap& tm_chi32,
                          const CUtensorMap& tm_clo32, const CUtensorMap& tm_w2, const CUtensorMap& tm_y,
                          const Gemm2Args& args, int grid, cudaStream_t s);
-cudaError_t launch_gemm1_pair(const CUtensorMap& tm_a, const CUtensorMap& tm_a32, const CUtensorMap& tm_w13,
-                              const Gemm1Args& args, int grid, cudaStream_t s);
-cudaError_t launch_gemm2_pair(const CUtensorMap& tm_chi, const CUtensorMap& tm_clo, const CUtensorMap& tm_chi32,
-                              const CUtensorMap& tm_clo32, const CUtensorMap& tm_w2, const Gemm2Args& args, int grid,
-                              cudaStream_t s);
 // Split-K finish of GEMM1 (sum of the splits, SwiGLU, hi/lo encoding).
 cudaError_t launch_swiglu_quant(const Gemm1Args& g, int grid, cudaStream_t s);
 cudaError_t gemm_set_attributes();
-cudaError_t gemm_pair_set_attributes();
-// Co-resident 2-CTA clusters of the pair kernels on the current device (0 if unknown).
-int gemm_pair_max_clusters();
 
 }  // namespace kf

@@ -16,15 +16,6 @@
 
 namespace kf {
 
-bool pdl_enabled() {
-  static const bool on = [] {
-    const char* v = getenv("KF_MOE_PDL");
-    return !(v && v[0] == '0');
-  }();
-  return on;
-}
-
-
 namespace {
 
 constexpr size_t kAlign = 256;
@@ -34,7 +25,6 @@ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 struct DeviceInfo {
   bool ready = false;
   int num_sms = 0;
-  int pair_clusters = 0;  // co-resident 2-CTA clusters of the CTA-pair GEMMs (0: use single-CTA GEMMs)
   int status = KF_OK;
 };
 
@@ -74,17 +64,7 @@ struct ProfScope {
   }
 };
 
-// KF_MOE_GEMM=pair selects the CTA-pair (cta_group::2) GEMMs; the default is the
-// single-CTA GEMMs.  The pair kernels move a third fewer bytes per SM, but the
-// per-K-chunk promotion handshake then crosses SMs (commit multicast to the peer,
-// remote arrival back) and, with two TMEM partial buffers, that latency is not
-// hidden: measured ~1.7x slower on B200, so they are opt-in.
-bool pair_gemms_requested() {
-  const char* v = getenv("KF_MOE_GEMM");
-  return v && strcmp(v, "pair") == 0;
-}
-
-int ensure_device(int* num_sms, int* pair_clusters = nullptr) {
+int ensure_device(int* num_sms) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return KF_ERR_CUDA;
   std::lock_guard<std::mutex> lock(g_mu);
@@ -96,15 +76,11 @@ int ensure_device(int* num_sms, int* pair_clusters = nullptr) {
     cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev);
     if (major != 10 || minor != 0) {
       d.status = KF_ERR_UNSUPPORTED_DEVICE;
-    } else if (gemm_set_attributes() != cudaSuccess || gemm_pair_set_attributes() != cudaSuccess) {
+    } else if (gemm_set_attributes() != cudaSuccess) {
       d.status = KF_ERR_CUDA;
     } else {
       d.status = KF_OK;
-      d.pair_clusters = pair_gemms_requested() ? gemm_pair_max_clusters() : 0;
     }
-    if (getenv("KF_MOE_DEBUG"))
-      fprintf(stderr, "kf_moe: device %d sms=%d pair_clusters=%d status=%d\n", dev, d.num_sms, d.pair_clusters,
-              d.status);
     if (!g_encode && d.status == KF_OK) {
       void* fn = nullptr;
       cudaDriverEntryPointQueryResult q;
@@ -118,7 +94,6 @@ int ensure_device(int* num_sms, int* pair_clusters = nullptr) {
     d.ready = true;
   }
   *num_sms = d.num_sms;
-  if (pair_clusters) *pair_clusters = d.pair_clusters;
   return d.status;
 }
 
@@ -190,16 +165,14 @@ constexpr int kSmallT = 32;
 // GEMMs and the reduce, from chunk masks already in the workspace.
 int run_experts(const Workspace& w, void* ws, const RowLayout& in, const void* w13, const float* w13_scale,
                 const void* w2, const float* w2_scale, int T, int E, int offset, void* out, int out_fp32, int num_sms,
-                int pair_clusters, bool front_done, cudaStream_t s, const PeerOut& po = PeerOut{nullptr, nullptr, 0, 1}) {
+                bool front_done, cudaStream_t s, const PeerOut& po = PeerOut{nullptr, nullptr, 0, 1}) {
   int* status = ws_ptr<int>(ws, w.status);
   Meta* meta = ws_ptr<Meta>(ws, w.meta);
   if (!front_done) {
     ProfScope ps(KF_KERNEL_PERMUTE_SCAN, s);
     if (launch_permute_scan(ws_ptr<uint4>(ws, w.chunk_masks), w.nchunk, E, meta, ws_ptr<int32_t>(ws, w.chunk_base),
                             ws_ptr<int32_t>(ws, w.tile_expert), ws_ptr<int32_t>(ws, w.tile_row0),
-                            ws_ptr<int32_t>(ws, w.tile_rows), ws_ptr<int32_t>(ws, w.ptile_expert),
-                            ws_ptr<int32_t>(ws, w.ptile_row0), ws_ptr<int32_t>(ws, w.ptile_rows), w.nt_cap, status,
-                            s) != cudaSuccess)
+                            ws_ptr<int32_t>(ws, w.tile_rows), w.nt_cap, status, s) != cudaSuccess)
       return KF_ERR_CUDA;
   }
   if (!front_done) {
@@ -230,17 +203,9 @@ int run_experts(const Workspace& w, void* ws, const RowLayout& in, const void* w
       !encode_u8_2d(&tm_clo32, ws_ptr<uint8_t>(ws, w.c_lo), kI, w.p_cap, kBlk, 32) ||
       !encode_u8_2d(&tm_w2, w2, kI, static_cast<uint64_t>(E) * kH, kBlk, 256))
     return KF_ERR_INVALID_ARGUMENT;
-  // The CTA-pair GEMM2 loads half of the 256-row W2 tile per CTA: a 128-row box
-  // (its shared-memory slot holds exactly 128 rows).
-  CUtensorMap tm_w2_half;
-  if (pair_clusters > 0 && !encode_u8_2d(&tm_w2_half, w2, kI, static_cast<uint64_t>(E) * kH, kBlk, kBlk))
-    return KF_ERR_INVALID_ARGUMENT;
-
-  // CTA-pair GEMMs walk 256-row pair tiles, single-CTA GEMMs 128-row tiles.
-  const bool pair = pair_clusters > 0;
-  const int32_t* t_exp = ws_ptr<int32_t>(ws, pair ? w.ptile_expert : w.tile_expert);
-  const int32_t* t_row0 = ws_ptr<int32_t>(ws, pair ? w.ptile_row0 : w.tile_row0);
-  const int32_t* t_rows = ws_ptr<int32_t>(ws, pair ? w.ptile_rows : w.tile_rows);
+  const int32_t* t_exp = ws_ptr<int32_t>(ws, w.tile_expert);
+  const int32_t* t_row0 = ws_ptr<int32_t>(ws, w.tile_row0);
+  const int32_t* t_rows = ws_ptr<int32_t>(ws, w.tile_rows);
   Gemm1Args g1;
   g1.meta = meta;
   g1.tile_expert = t_exp;
@@ -253,22 +218,15 @@ int run_experts(const Workspace& w, void* ws, const RowLayout& in, const void* w
   g1.c_scale = ws_ptr<float>(ws, w.c_scale);
   g1.p_cap = w.p_cap;
   g1.status = status;
-  g1.ksplit = pair ? 1 : w.ksplit1;
+  g1.ksplit = w.ksplit1;
   g1.max_pairs = T * kTopK;
   g1.slot_pair = ws_ptr<int32_t>(ws, w.slot_pair);
   g1.partial = ws_ptr<float>(ws, w.partial);
   {
     ProfScope ps(KF_KERNEL_GEMM1, s);
-    cudaError_t e;
-    if (pair) {
-      const int units = w.nt_cap * kIB;
-      const int clusters = units < pair_clusters ? units : pair_clusters;
-      e = launch_gemm1_pair(tm_a, tm_a32, tm_w13, g1, 2 * clusters, s);
-    } else {
-      const int units = w.nt_cap * kIB * g1.ksplit;
-      e = launch_gemm1(tm_a, tm_a32, tm_w13, g1, units < num_sms ? units : num_sms, s);
-    }
-    if (e != cudaSuccess) return KF_ERR_CUDA;
+    const int units = w.nt_cap * kIB * g1.ksplit;
+    if (launch_gemm1(tm_a, tm_a32, tm_w13, g1, units < num_sms ? units : num_sms, s) != cudaSuccess)
+      return KF_ERR_CUDA;
   }
   if (g1.ksplit > 1) {
     ProfScope ps(KF_KERNEL_SWIGLU_QUANT, s);
@@ -289,22 +247,18 @@ int run_experts(const Workspace& w, void* ws, const RowLayout& in, const void* w
 
   {
     ProfScope ps(KF_KERNEL_GEMM2, s);
-    cudaError_t e;
     const int units = w.nt_cap * (kH / 256);
-    if (pair) {
-      const int clusters = units < pair_clusters ? units : pair_clusters;
-      e = launch_gemm2_pair(tm_chi, tm_clo, tm_chi32, tm_clo32, tm_w2_half, g2, 2 * clusters, s);
-    } else {
-      CUtensorMap tm_y;
-      if (!encode_2d(&tm_y, ws_ptr<float>(ws, w.y), 4, kH, w.p_cap, 32, 32)) return KF_ERR_INVALID_ARGUMENT;
-      e = launch_gemm2(tm_chi, tm_clo, tm_chi32, tm_clo32, tm_w2, tm_y, g2, units < num_sms ? units : num_sms, s);
-    }
-    if (e != cudaSuccess) return KF_ERR_CUDA;
+    CUtensorMap tm_y;
+    if (!encode_2d(&tm_y, ws_ptr<float>(ws, w.y), 4, kH, w.p_cap, 32, 32)) return KF_ERR_INVALID_ARGUMENT;
+    if (launch_gemm2(tm_chi, tm_clo, tm_chi32, tm_clo32, tm_w2, tm_y, g2, units < num_sms ? units : num_sms, s) !=
+        cudaSuccess)
+      return KF_ERR_CUDA;
   }
 
   {
     ProfScope ps(KF_KERNEL_REDUCE, s);
-    if (launch_reduce(ws_ptr<int32_t>(ws, w.token_slot), ws_ptr<float>(ws, w.y), T, out, out_fp32, po, s) !=
+    if (launch_reduce(ws_ptr<int32_t>(ws, w.token_slot), ws_ptr<float>(ws, w.y), T, out, out_fp32, po, 4 * num_sms,
+                      s) !=
         cudaSuccess)
       return KF_ERR_CUDA;
   }
@@ -317,8 +271,7 @@ int run_front_small(const Workspace& w, void* ws, const float* logits, const voi
   return launch_front_small(logits, bias, rsf, in, T, E, offset, w.p_cap, ws_ptr<Meta>(ws, w.meta),
                             ws_ptr<int32_t>(ws, w.tile_expert),
                             ws_ptr<int32_t>(ws, w.tile_row0), ws_ptr<int32_t>(ws, w.tile_rows),
-                            ws_ptr<int32_t>(ws, w.ptile_expert), ws_ptr<int32_t>(ws, w.ptile_row0),
-                            ws_ptr<int32_t>(ws, w.ptile_rows), ws_ptr<int32_t>(ws, w.token_slot),
+                            ws_ptr<int32_t>(ws, w.token_slot),
                             ws_ptr<int32_t>(ws, w.slot_token), ws_ptr<float>(ws, w.slot_weight),
                             ws_ptr<int32_t>(ws, w.slot_pair), ws_ptr<uint8_t>(ws, w.a_rows),
                             ws_ptr<float>(ws, w.a_scale), ws_ptr<int>(ws, w.status), s) == cudaSuccess
@@ -331,9 +284,7 @@ int run_front_small(const Workspace& w, void* ws, const float* logits, const voi
 Workspace plan_workspace(int32_t T, int32_t E) {
   Workspace w{};
   const int64_t pairs_max = static_cast<int64_t>(T) * (E < kTopK ? E : kTopK);
-  // + one tile of slack: the last 256-row pair tile may extend 128 rows past the last segment
-  const int64_t rows =
-      align_up(static_cast<size_t>(pairs_max + static_cast<int64_t>(E) * (kBlk - 1)), kBlk) + kBlk;
+  const int64_t rows = align_up(static_cast<size_t>(pairs_max + static_cast<int64_t>(E) * (kBlk - 1)), kBlk);
   w.p_cap = static_cast<int32_t>(rows);
   w.nt_cap = w.p_cap / kBlk;
   w.nchunk = (T + kChunkTokens - 1) / kChunkTokens;
@@ -355,9 +306,6 @@ Workspace plan_workspace(int32_t T, int32_t E) {
   w.tile_expert = take(static_cast<size_t>(w.nt_cap) * 4);
   w.tile_row0 = take(static_cast<size_t>(w.nt_cap) * 4);
   w.tile_rows = take(static_cast<size_t>(w.nt_cap) * 4);
-  w.ptile_expert = take(static_cast<size_t>(w.nt_cap) * 4);
-  w.ptile_row0 = take(static_cast<size_t>(w.nt_cap) * 4);
-  w.ptile_rows = take(static_cast<size_t>(w.nt_cap) * 4);
   w.slot_token = take(pc * 4);
   w.slot_weight = take(pc * 4);
   w.slot_pair = take(pc * 4);
@@ -437,8 +385,8 @@ int kf_moe_forward(const float* routing_logits, const void* routing_bias, const 
     return KF_ERR_INVALID_ARGUMENT;
   const Workspace w = plan_workspace(T, E);
   if (workspace_bytes < w.total) return KF_ERR_WORKSPACE_TOO_SMALL;
-  int sms = 0, pair_clusters = 0;
-  rc = ensure_device(&sms, &pair_clusters);
+  int sms = 0;
+  rc = ensure_device(&sms);
   if (rc != KF_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(ws_ptr<int>(workspace, w.status), 0, sizeof(int), s) != cudaSuccess) return KF_ERR_CUDA;
@@ -457,7 +405,7 @@ int kf_moe_forward(const float* routing_logits, const void* routing_bias, const 
       return KF_ERR_CUDA;
   }
   return run_experts(w, workspace, in, gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, T, E,
-                     local_expert_offset, output, 0, sms, pair_clusters, small, s);
+                     local_expert_offset, output, 0, sms, small, s);
 }
 
 }  // extern "C"
@@ -482,8 +430,8 @@ int experts_common(const RowLayout& in, const void* gemm1_weights, const float* 
     return KF_ERR_INVALID_ARGUMENT;
   const Workspace w = plan_workspace(T, E);
   if (workspace_bytes < w.total) return KF_ERR_WORKSPACE_TOO_SMALL;
-  int sms = 0, pair_clusters = 0;
-  rc = ensure_device(&sms, &pair_clusters);
+  int sms = 0;
+  rc = ensure_device(&sms);
   if (rc != KF_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int* status = ws_ptr<int>(workspace, w.status);
@@ -498,7 +446,7 @@ int experts_common(const RowLayout& in, const void* gemm1_weights, const float* 
       return KF_ERR_CUDA;
   }
   return run_experts(w, workspace, in, gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, T, E,
-                     offset, output, output_fp32 ? 1 : 0, sms, pair_clusters, small, s, po);
+                     offset, output, output_fp32 ? 1 : 0, sms, small, s, po);
 }
 
 }  // namespace

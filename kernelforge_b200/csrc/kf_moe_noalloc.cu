@@ -43,7 +43,12 @@ extern "C" int kf_moe_forward_noalloc(const float* routing_logits, const void* r
                                       const void* gemm2_weights, const float* gemm2_weights_scale,
                                       int32_t num_tokens, int32_t num_local_experts, int32_t local_expert_offset,
                                       float routed_scaling_factor, void* output, void* stream) {
-  if (num_tokens < 0 || num_local_experts < 1) return KF_ERR_INVALID_ARGUMENT;
+  // the checks kf_moe_forward makes on every call come first, so a call that is
+  // invalid there is invalid here too; the static array's own limits come after
+  if (num_tokens < 0 || num_tokens > KF_MOE_MAX_TOKENS || num_local_experts < 1 ||
+      num_local_experts > KF_MOE_GLOBAL_EXPERTS || local_expert_offset < 0 ||
+      local_expert_offset > KF_MOE_GLOBAL_EXPERTS - num_local_experts)
+    return KF_ERR_INVALID_ARGUMENT;
   if (num_tokens > KF_MOE_NOALLOC_MAX_TOKENS || num_local_experts > KF_MOE_NOALLOC_MAX_LOCAL_EXPERTS)
     return KF_ERR_EXCEEDS_STATIC_SCRATCH;
   if (num_tokens == 0) return KF_OK;
@@ -59,4 +64,21 @@ extern "C" int kf_moe_forward_noalloc(const float* routing_logits, const void* r
                         gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, num_tokens, num_local_experts,
                         local_expert_offset, routed_scaling_factor, output, scratch,
                         static_cast<size_t>(KF_MOE_NOALLOC_SCRATCH_BYTES), stream);
+}
+
+// The status word of kf_moe_forward_noalloc's calls sits at the start of the
+// static array (kf_moe_forward keeps it at offset 0 of its scratch): read it and
+// clear it on the stream, without allocating.
+extern "C" int kf_moe_noalloc_read_status(int32_t* status, void* stream) {
+  if (!status) return KF_ERR_INVALID_ARGUMENT;
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != KF_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t v = 0;
+  if (cudaMemcpyAsync(&v, scratch, sizeof(int32_t), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess || cudaMemsetAsync(scratch, 0, sizeof(int32_t), s) != cudaSuccess)
+    return KF_ERR_CUDA;
+  *status = v;
+  return v ? KF_ERR_DEVICE_STATUS : KF_OK;
 }

@@ -101,35 +101,6 @@ __device__ __forceinline__ bool mbar_wait_abort(uint64_t* bar, uint32_t parity, 
   }
 }
 
-// Cluster-scope acquire variant: for barriers that CTAs of the pair other than
-// the waiting one arrive on (remote arrivals, or TMA bytes of the peer CTA).
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-__device__ __forceinline__ bool mbar_wait_abort_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                                        int* status, int code) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (true) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    if (*abort_flag) return false;
-    if (clock64() - t0 > kWaitCycles) {
-      *abort_flag = 1;
-      record_error(status, code);
-      return false;
-    }
-  }
-}
-
 // --------------------------------------------------------------------- TMA --
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -263,79 +234,6 @@ __host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
          | (0u << 15) | (0u << 16)                   // A, B K-major
          | (static_cast<uint32_t>(N >> 3) << 17)     // N / 8
          | (static_cast<uint32_t>(M >> 4) << 24);    // M / 16
-}
-
-// ------------------------------------------------------- CTA pairs (2-SM) --
-// Two CTAs of a cluster share one tcgen05 MMA with M = 256: each holds 128 rows
-// of A and half of B in its own shared memory and receives its 128 rows of D in
-// its own tensor memory.  No load here uses cluster multicast; every CTA
-// fetches its own tiles (the commit below multicasts only its mbarrier arrival).
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-// Shared::cluster address of `local` (a shared::cta address) in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t local, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
-  return r;
-}
-
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// Tiled 2-D load into this CTA's shared memory whose completion (transaction
-// bytes) is counted on the pair leader's mbarrier (a shared::cluster address).
-__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, int32_t x, int32_t y,
-                                                 uint32_t leader_bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(leader_bar)
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t* holder, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(holder)),
-               "r"(ncols)
-               : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-
-// D (+)= A * B^T over the CTA pair: M = 256 (128 rows per CTA), operands read
-// from the same shared-memory offsets in both CTAs.
-__device__ __forceinline__ void mma_f8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                            uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Arrive once on the mbarrier at the same offset in every CTA of `cta_mask` when
-// the pair's previously issued tcgen05 operations have completed.
-__device__ __forceinline__ void mma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-          smem_u32(bar)),
-      "h"(cta_mask)
-      : "memory");
-}
-
-__device__ __forceinline__ void named_barrier_sync(int id, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 template <int N>

@@ -199,17 +199,14 @@ __device__ __forceinline__ int popc4(uint4 m) { return __popc(m.x) + __popc(m.y)
 
 // One block; thread e owns local expert e.  Running counts over chunks give each
 // chunk's base inside the expert's segment (stable: chunk order = token order).
-// Each expert's rows are one 128-aligned segment; it is cut into 128-row tiles
-// (single-CTA GEMMs) and 256-row pair tiles (CTA-pair GEMMs).
+// Each expert's rows are one 128-aligned segment, cut into 128-row tiles.
 __global__ void __launch_bounds__(kMaxLocalExperts) permute_scan_kernel(
     const uint4* __restrict__ chunk_masks, int nchunk, int E, Meta* __restrict__ meta,
     int32_t* __restrict__ chunk_base, int32_t* __restrict__ tile_expert, int32_t* __restrict__ tile_row0,
-    int32_t* __restrict__ tile_rows, int32_t* __restrict__ ptile_expert, int32_t* __restrict__ ptile_row0,
-    int32_t* __restrict__ ptile_rows, int nt_cap, int* status) {
+    int32_t* __restrict__ tile_rows, int nt_cap, int* status) {
   grid_dep_wait();
   grid_dep_trigger();
   __shared__ int32_t tiles_scan[kMaxLocalExperts];
-  __shared__ int32_t ptiles_scan[kMaxLocalExperts];
   __shared__ int32_t pairs_scan[kMaxLocalExperts];
   const int e = threadIdx.x;
   int run = 0;
@@ -235,26 +232,20 @@ __global__ void __launch_bounds__(kMaxLocalExperts) permute_scan_kernel(
     }
   }
   const int ntiles = (run + kBlk - 1) / kBlk;
-  const int nptiles = (run + 2 * kBlk - 1) / (2 * kBlk);
   tiles_scan[e] = ntiles;
-  ptiles_scan[e] = nptiles;
   pairs_scan[e] = run;
   __syncthreads();
   // inclusive Hillis-Steele scans over 256 entries
   for (int off = 1; off < kMaxLocalExperts; off <<= 1) {
     const int a = (e >= off) ? tiles_scan[e - off] : 0;
     const int b = (e >= off) ? pairs_scan[e - off] : 0;
-    const int c = (e >= off) ? ptiles_scan[e - off] : 0;
     __syncthreads();
     tiles_scan[e] += a;
     pairs_scan[e] += b;
-    ptiles_scan[e] += c;
     __syncthreads();
   }
   const int tstart = tiles_scan[e] - ntiles;
-  const int pstart = ptiles_scan[e] - nptiles;
   const int total_tiles = tiles_scan[kMaxLocalExperts - 1];
-  const int total_ptiles = ptiles_scan[kMaxLocalExperts - 1];
   if (e < E) {
     meta->expert_count[e] = run;
     meta->expert_pad_start[e] = tstart * kBlk;
@@ -268,20 +259,9 @@ __global__ void __launch_bounds__(kMaxLocalExperts) permute_scan_kernel(
       tile_row0[ti] = ti * kBlk;
       tile_rows[ti] = min(kBlk, run - i * kBlk);
     }
-    for (int i = 0; i < nptiles; ++i) {
-      const int pi = pstart + i;
-      if (pi >= nt_cap) {
-        record_error(status, KF_STATUS_SLOT_OVERFLOW);
-        break;
-      }
-      ptile_expert[pi] = e;
-      ptile_row0[pi] = tstart * kBlk + i * 2 * kBlk;
-      ptile_rows[pi] = min(2 * kBlk, run - i * 2 * kBlk);
-    }
   }
   if (e == 0) {
     meta->num_tiles = min(total_tiles, nt_cap);
-    meta->num_ptiles = min(total_ptiles, nt_cap);
     meta->num_pairs = pairs_scan[kMaxLocalExperts - 1];
   }
 }
@@ -374,7 +354,6 @@ __global__ void __launch_bounds__(kFrontThreads) front_small_kernel(
     const float* __restrict__ logits, const __nv_bfloat16* __restrict__ bias, float rsf, const RowLayout in, int T,
     int E, int offset, int p_cap, Meta* __restrict__ meta,
     int32_t* __restrict__ tile_expert, int32_t* __restrict__ tile_row0, int32_t* __restrict__ tile_rows,
-    int32_t* __restrict__ ptile_expert, int32_t* __restrict__ ptile_row0, int32_t* __restrict__ ptile_rows,
     int32_t* __restrict__ token_slot, int32_t* __restrict__ slot_token, float* __restrict__ slot_weight,
     int32_t* __restrict__ slot_pair, uint8_t* __restrict__ a_rows, float* __restrict__ a_scale, int* status) {
   grid_dep_wait();
@@ -450,15 +429,9 @@ __global__ void __launch_bounds__(kFrontThreads) front_small_kernel(
         tile_expert[tstart] = tid;
         tile_row0[tstart] = tstart * kBlk;
         tile_rows[tstart] = cnt;
-        ptile_expert[tstart] = tid;
-        ptile_row0[tstart] = tstart * kBlk;
-        ptile_rows[tstart] = cnt;
       }
     }
-    if (tid == 0) {
-      meta->num_tiles = total;
-      meta->num_ptiles = total;
-    }
+    if (tid == 0) meta->num_tiles = total;
   }
   __syncthreads();
   if (tid == 0) meta->num_pairs = total_pairs;
@@ -500,73 +473,98 @@ __global__ void __launch_bounds__(kFrontThreads) front_small_kernel(
 }
 
 // out[t] = sum of the token's permuted rows of y (already routing-weighted), in
-// ascending row order (= ascending local expert, the reference's index_add_ order).
-__global__ void __launch_bounds__(256) unpermute_reduce_kernel(const int32_t* __restrict__ token_slot,
+// ascending row order (= ascending local expert, the reference's index_add_ order),
+// accumulated in fp32 and rounded once.  CTAs stride over the rows; a thread owns
+// 8 consecutive columns (two 16-byte loads per row of y, one 16-byte store).
+constexpr int kReduceThreads = 224;   // 7 warps: a row's 896 column groups in 4 passes
+constexpr int kMaxWorld = 64;
+
+__global__ void __launch_bounds__(kReduceThreads) unpermute_reduce_kernel(const int32_t* __restrict__ token_slot,
                                                      const float* __restrict__ y, int T, void* __restrict__ out,
                                                      int out_fp32, const PeerOut po) {
   grid_dep_wait();
-  const int t = blockIdx.x;
-  __shared__ __nv_bfloat16* peer_row;
+  // Peer return: received row t came from source s (sources in rank order) as the
+  // j-th of s's rows for this rank; it goes back to row (s's rows for lower ranks)
+  // + j of s's return buffer.  Each CTA builds the map once: src_end[s] = received
+  // rows of sources <= s, src_base[s] = (return row) - (received row) for source s.
+  __shared__ int32_t src_end[kMaxWorld];
+  __shared__ int32_t src_base[kMaxWorld];
   if (po.peer_back) {
-    // received row t came from source s (sources in rank order) as its j-th row
-    // for this rank; it returns to row (s's rows for lower ranks) + j of s's buffer.
-    // A row past the received total (T larger than the count matrix says) has no
-    // place in any source's send order and is not stored.
-    if (threadIdx.x == 0) {
-      int s = 0, off = 0;
-      while (s + 1 < po.world && off + po.counts[s * po.world + po.rank] <= t) {
-        off += po.counts[s * po.world + po.rank];
-        ++s;
-      }
-      int so = 0;
+    const int s = threadIdx.x;
+    int n = 0, so = 0;
+    if (s < po.world) {
+      n = po.counts[s * po.world + po.rank];
       for (int d = 0; d < po.rank; ++d) so += po.counts[s * po.world + d];
-      peer_row = t - off < po.counts[s * po.world + po.rank]
-                     ? static_cast<__nv_bfloat16*>(po.peer_back[s]) + (static_cast<size_t>(so) + (t - off)) * kH
-                     : nullptr;
+      src_end[s] = n;
+      src_base[s] = so;
     }
     __syncthreads();
-    if (peer_row == nullptr) return;  // uniform over the block
-  }
-  int sl[8];
-  int n = 0;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const int v = token_slot[static_cast<size_t>(t) * kTopK + k];
-    sl[k] = v < 0 ? 0x7fffffff : v;
-    n += v >= 0 ? 1 : 0;
-  }
-  // sort ascending (8-element odd-even transposition network)
-#pragma unroll
-  for (int r = 0; r < 8; ++r) {
-#pragma unroll
-    for (int k = (r & 1); k + 1 < 8; k += 2) {
-      const int a = sl[k], b = sl[k + 1];
-      sl[k] = min(a, b);
-      sl[k + 1] = max(a, b);
-    }
-  }
-  for (int c = threadIdx.x; c < kH / 4; c += blockDim.x) {
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      if (k < n) {
-        const float4 v = reinterpret_cast<const float4*>(y + static_cast<size_t>(sl[k]) * kH)[c];
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
+    if (threadIdx.x == 0) {
+      int off = 0;
+      for (int q = 0; q < po.world; ++q) {
+        src_base[q] -= off;
+        off += src_end[q];
+        src_end[q] = off;
       }
     }
-    if (out_fp32) {
-      reinterpret_cast<float4*>(static_cast<float*>(out) + static_cast<size_t>(t) * kH)[c] = acc;
-    } else {
-      __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
-      __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
-      uint2 packed;
-      packed.x = *reinterpret_cast<uint32_t*>(&lo);
-      packed.y = *reinterpret_cast<uint32_t*>(&hi);
-      __nv_bfloat16* row = po.peer_back ? peer_row : static_cast<__nv_bfloat16*>(out) + static_cast<size_t>(t) * kH;
-      reinterpret_cast<uint2*>(row)[c] = packed;
+    __syncthreads();
+  }
+  for (int t = blockIdx.x; t < T; t += gridDim.x) {
+    uint4* dst16 = nullptr;
+    if (po.peer_back) {
+      // a row past the received total (T larger than the count matrix says) has no
+      // place in any source's send order and is not stored; uniform over the block
+      int s = 0;
+      while (s < po.world && t >= src_end[s]) ++s;
+      if (s == po.world) continue;
+      dst16 = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(po.peer_back[s]) +
+                                       static_cast<size_t>(src_base[s] + t) * kH);
+    } else if (!out_fp32) {
+      dst16 = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + static_cast<size_t>(t) * kH);
+    }
+    int sl[8];
+    int n = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int v = token_slot[static_cast<size_t>(t) * kTopK + k];
+      sl[k] = v < 0 ? 0x7fffffff : v;
+      n += v >= 0 ? 1 : 0;
+    }
+    // sort ascending (8-element odd-even transposition network)
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+#pragma unroll
+      for (int k = (r & 1); k + 1 < 8; k += 2) {
+        const int a = sl[k], b = sl[k + 1];
+        sl[k] = min(a, b);
+        sl[k + 1] = max(a, b);
+      }
+    }
+    for (int g = threadIdx.x; g < kH / 8; g += blockDim.x) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (k < n) {
+          const float4* src = reinterpret_cast<const float4*>(y + static_cast<size_t>(sl[k]) * kH) + 2 * g;
+          const float4 a = src[0], b = src[1];
+          acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+          acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+        }
+      }
+      if (dst16) {
+        uint4 packed;
+        __nv_bfloat162 h0 = __floats2bfloat162_rn(acc[0], acc[1]), h1 = __floats2bfloat162_rn(acc[2], acc[3]);
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(acc[4], acc[5]), h3 = __floats2bfloat162_rn(acc[6], acc[7]);
+        packed.x = *reinterpret_cast<uint32_t*>(&h0);
+        packed.y = *reinterpret_cast<uint32_t*>(&h1);
+        packed.z = *reinterpret_cast<uint32_t*>(&h2);
+        packed.w = *reinterpret_cast<uint32_t*>(&h3);
+        dst16[g] = packed;
+      } else {
+        float4* d = reinterpret_cast<float4*>(static_cast<float*>(out) + static_cast<size_t>(t) * kH) + 2 * g;
+        d[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        d[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+      }
     }
   }
   if (po.peer_back) __threadfence_system();
@@ -594,11 +592,10 @@ cudaError_t launch_masks_from_topk(const RowLayout& in, int T, int E, int offset
 }
 
 cudaError_t launch_permute_scan(const uint4* chunk_masks, int nchunk, int E, Meta* meta, int32_t* chunk_base,
-                                int32_t* tile_expert, int32_t* tile_row0, int32_t* tile_rows, int32_t* ptile_expert,
-                                int32_t* ptile_row0, int32_t* ptile_rows, int nt_cap, int* status, cudaStream_t s) {
-  return launch_chained(permute_scan_kernel, dim3(1), dim3(kMaxLocalExperts), 0, s, chunk_masks, nchunk, E, meta, chunk_base, tile_expert,
-                                                     tile_row0, tile_rows, ptile_expert, ptile_row0, ptile_rows,
-                                                     nt_cap, status);
+                                int32_t* tile_expert, int32_t* tile_row0, int32_t* tile_rows, int nt_cap, int* status,
+                                cudaStream_t s) {
+  return launch_chained(permute_scan_kernel, dim3(1), dim3(kMaxLocalExperts), 0, s, chunk_masks, nchunk, E, meta,
+                        chunk_base, tile_expert, tile_row0, tile_rows, nt_cap, status);
 }
 
 cudaError_t launch_permute_assign(const RowLayout& in, const uint4* chunk_masks, const int32_t* chunk_base,
@@ -612,14 +609,11 @@ cudaError_t launch_permute_assign(const RowLayout& in, const uint4* chunk_masks,
 
 cudaError_t launch_front_small(const float* logits, const void* bias, float rsf, const RowLayout& in, int T, int E,
                                int offset, int p_cap, Meta* meta, int32_t* tile_expert, int32_t* tile_row0,
-                               int32_t* tile_rows, int32_t* ptile_expert, int32_t* ptile_row0, int32_t* ptile_rows,
-                               int32_t* token_slot, int32_t* slot_token, float* slot_weight, int32_t* slot_pair,
-                               uint8_t* a_rows, float* a_scale, int* status, cudaStream_t s) {
-  return launch_chained(front_small_kernel, dim3(1), dim3(kFrontThreads), 0, s, logits, static_cast<const __nv_bfloat16*>(bias), rsf, in, T, E,
-                                                 offset, p_cap, meta,
-                                                 tile_expert, tile_row0, tile_rows, ptile_expert, ptile_row0,
-                                                 ptile_rows, token_slot, slot_token, slot_weight, slot_pair, a_rows,
-                                                 a_scale, status);
+                               int32_t* tile_rows, int32_t* token_slot, int32_t* slot_token, float* slot_weight,
+                               int32_t* slot_pair, uint8_t* a_rows, float* a_scale, int* status, cudaStream_t s) {
+  return launch_chained(front_small_kernel, dim3(1), dim3(kFrontThreads), 0, s, logits,
+                        static_cast<const __nv_bfloat16*>(bias), rsf, in, T, E, offset, p_cap, meta, tile_expert,
+                        tile_row0, tile_rows, token_slot, slot_token, slot_weight, slot_pair, a_rows, a_scale, status);
 }
 
 cudaError_t launch_gather_rows(const Meta* meta, const int32_t* tile_rows, const int32_t* slot_token,
@@ -629,8 +623,10 @@ cudaError_t launch_gather_rows(const Meta* meta, const int32_t* tile_rows, const
 }
 
 cudaError_t launch_reduce(const int32_t* token_slot, const float* y, int T, void* out, int out_fp32, const PeerOut& po,
-                          cudaStream_t s) {
-  return launch_chained(unpermute_reduce_kernel, dim3(T), dim3(256), 0, s, token_slot, y, T, out, out_fp32, po);
+                          int grid, cudaStream_t s) {
+  if (po.peer_back && (po.world < 1 || po.world > kMaxWorld)) return cudaErrorInvalidValue;
+  return launch_chained(unpermute_reduce_kernel, dim3(T < grid ? T : grid), dim3(kReduceThreads), 0, s, token_slot, y,
+                        T, out, out_fp32, po);
 }
 
 }  // namespace kf

@@ -22,16 +22,14 @@ destination's receive area and the expert stage's reduce kernel writes each
 partial back into its source's return area, with the library's bounded barrier
 between the phases; reading the count matrix is the one host synchronisation
 of a step.
-With ``plumbing="cuda"`` the same kernels run around ``torch.distributed``
-all-to-alls over NCCL (split sizes first, then rows).  The tensor-op functions
-below restate the data flow for the CPU tests.
+With ``exchange="nccl"`` the same kernels run around ``torch.distributed``
+all-to-alls over NCCL (split sizes first, then rows).
 """
 from __future__ import annotations
 
 import ctypes
 import os
-from dataclasses import dataclass
-from typing import Callable, Optional
+from typing import Optional
 
 import torch
 import torch.distributed as dist
@@ -41,65 +39,6 @@ HB = H // 128
 E_GLOBAL = 256
 TOP_K = 8
 ROW_BYTES = H + HB * 4 + TOP_K * 4 + TOP_K * 4   # 7456: fp8 row | 56 scales | 8 ids | 8 weights
-
-
-@dataclass
-class DispatchPlan:
-    send_counts: torch.Tensor   # int64 [N]: rows sent to each rank
-    send_token: torch.Tensor    # int64 [S]: source token of each send row (grouped by destination)
-    send_ids: torch.Tensor      # int32 [S, 8]: expert ids, -1 where the destination does not own the expert
-    send_w: torch.Tensor        # f32 [S, 8]
-    pos: torch.Tensor           # int64 [T, N]: row of (token, destination) in the send buffer, -1 if not sent
-
-
-def dispatch_plan(topk_idx: torch.Tensor, topk_w: torch.Tensor, world: int) -> DispatchPlan:
-    """Which rows go to which rank, deduplicated per (token, destination), token order kept."""
-    T = topk_idx.shape[0]
-    per_rank = E_GLOBAL // world
-    ids = topk_idx.to(torch.int64)
-    dest = ids // per_rank                                               # [T, 8]
-    member = torch.zeros(T, world, dtype=torch.bool, device=ids.device)
-    member.scatter_(1, dest, True)
-    send_counts = member.sum(dim=0)
-    # destination-major, token-ascending order
-    d_idx, t_idx = torch.nonzero(member.t(), as_tuple=True)
-    pos = torch.full((T, world), -1, dtype=torch.int64, device=ids.device)
-    pos[t_idx, d_idx] = torch.arange(t_idx.numel(), device=ids.device)
-    own = dest[t_idx] == d_idx.unsqueeze(1)
-    send_ids = torch.where(own, ids[t_idx], torch.full_like(ids[t_idx], -1)).to(torch.int32)
-    send_w = torch.where(own, topk_w[t_idx].to(torch.float32), torch.zeros_like(topk_w[t_idx], dtype=torch.float32))
-    return DispatchPlan(send_counts, t_idx, send_ids, send_w, pos)
-
-
-def pack_rows(hidden: torch.Tensor, hidden_scale: torch.Tensor, plan: DispatchPlan) -> torch.Tensor:
-    """[S, 7456] uint8 rows: hidden fp8 | scales f32 [56] | ids int32 [8] | weights f32 [8]."""
-    tok = plan.send_token
-    parts = [hidden.index_select(0, tok).view(torch.uint8),
-             hidden_scale.t().index_select(0, tok).contiguous().view(torch.uint8),
-             plan.send_ids.contiguous().view(torch.uint8),
-             plan.send_w.contiguous().view(torch.uint8)]
-    return torch.cat(parts, dim=1)
-
-
-def unpack_rows(rows: torch.Tensor):
-    """Inverse of pack_rows: (hidden e4m3 [R,7168], scales f32 [56,R], ids int32 [R,8], w f32 [R,8])."""
-    hid = rows[:, :H].contiguous().view(torch.float8_e4m3fn)
-    sc = rows[:, H:H + HB * 4].contiguous().view(torch.float32).t().contiguous()
-    ids = rows[:, H + HB * 4:H + HB * 4 + TOP_K * 4].contiguous().view(torch.int32)
-    w = rows[:, H + HB * 4 + TOP_K * 4:].contiguous().view(torch.float32)
-    return hid, sc, ids, w
-
-
-def combine(back: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
-    """out[t] = sum over destinations d (ascending) of back[pos[t, d]]; fp32 sum, one bf16 rounding."""
-    T, world = pos.shape
-    acc = torch.zeros(T, H, dtype=torch.float32, device=back.device)
-    for d in range(world):
-        p = pos[:, d]
-        sel = torch.nonzero(p >= 0).flatten()
-        if sel.numel():
-            acc.index_copy_(0, sel, acc.index_select(0, sel) + back.index_select(0, p[sel]).to(torch.float32))
-    return acc.to(torch.bfloat16)
 
 
 class PeerExchange:
@@ -189,17 +128,10 @@ def _exchange_counts(send_counts: torch.Tensor, group) -> torch.Tensor:
 
 
 class ExpertParallelMoE:
-    """One rank's share of the expert-parallel layer.
-
-    ``experts_fn`` / ``route_fn`` default to the CUDA entry points
-    (``binding.experts`` / ``binding.route``); the CPU multi-process tests pass
-    reference implementations to exercise the data flow on gloo ranks.
-    """
+    """One rank's share of the expert-parallel layer (CUDA routing, exchange and expert kernels)."""
 
     def __init__(self, weights, local_expert_offset: int, num_local: int, group=None,
-                 combine_dtype: torch.dtype = torch.bfloat16,
-                 experts_fn: Optional[Callable] = None, route_fn: Optional[Callable] = None,
-                 plumbing: str = "p2p"):
+                 combine_dtype: torch.dtype = torch.bfloat16, exchange: str = "p2p"):
         self.w = weights
         self.offset = int(local_expert_offset)
         self.num_local = int(num_local)
@@ -209,22 +141,15 @@ class ExpertParallelMoE:
         if self.num_local * self.world != E_GLOBAL or self.offset != self.rank * self.num_local:
             raise ValueError("expert-parallel shards must be equal, contiguous and in rank order")
         self.combine_dtype = combine_dtype
-        if experts_fn is None or route_fn is None:
-            from . import binding
-            experts_fn = experts_fn or binding.experts
-            route_fn = route_fn or binding.route
-        self.experts_fn = experts_fn
-        self.route_fn = route_fn
         # "p2p": dispatch rows and returned partials stored straight into the peers'
         # symmetric buffers by the library's kernels (kf_ep_*_p2p), bounded device
-        # barriers in place of the two NCCL all-to-alls; "cuda": the same kernels
-        # around NCCL all_to_all_single; "torch": the tensor-op restatement above,
-        # used by the CPU multi-process tests to check the data flow on gloo ranks
-        if plumbing not in ("p2p", "cuda", "torch"):
-            raise ValueError("plumbing must be 'p2p', 'cuda' or 'torch'")
-        if plumbing == "p2p" and combine_dtype != torch.bfloat16:
+        # barriers in place of the two all-to-alls; "nccl": the same kernels around
+        # NCCL all_to_all_single
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError("exchange must be 'p2p' or 'nccl'")
+        if exchange == "p2p" and combine_dtype != torch.bfloat16:
             raise ValueError("the peer-to-peer exchange returns bf16 partials")
-        self.plumbing = plumbing
+        self.exchange = exchange
         self._peer = None
 
     def local_pairs(self) -> int:
@@ -241,41 +166,38 @@ class ExpertParallelMoE:
         the device.  ``forward`` runs the same check when it reads the next step's count matrix, so a
         failure in a step's pack or return barrier surfaces one step later at the latest; calling
         this after a step reports it at once.  The status is sticky: once set, every later step
-        raises, since the exchange can no longer be trusted.  No-op for the NCCL and CPU plumbings
-        (their collectives raise their own errors)."""
+        raises, since the exchange can no longer be trusted.  No-op for the NCCL exchange (its
+        collectives raise their own errors)."""
         err = peer_status_error(self.status())
         if err:
             raise RuntimeError(err)
 
     def status(self) -> int:
-        """The peer exchange's device status word (0: no failure; synchronises), 0 for other plumbings."""
-        if self.plumbing != "p2p" or self._peer is None:
+        """The peer exchange's device status word (0: no failure; synchronises), 0 for the NCCL exchange."""
+        if self.exchange != "p2p" or self._peer is None:
             return 0
         return int(self._peer.status.item())
 
     def forward(self, routing_logits, routing_bias, hidden_states, hidden_states_scale, routed_scaling_factor):
         """The layer on this rank's tokens.  ``hidden_states`` are e4m3 with ``hidden_states_scale``
         ``[56, T]``, or bf16 rows with ``hidden_states_scale=None``: then the peer exchange quantises
-        each row as it packs it (the other plumbings quantise the rows first).  With the peer
+        each row as it packs it (the NCCL exchange quantises the rows first).  With the peer
         exchange, a failed barrier of this step's later phases raises at the next step or at
         ``check()``."""
-        if hidden_states_scale is None and self.plumbing != "p2p":
-            from . import binding as B
+        from . import binding as B
+        if hidden_states_scale is None and self.exchange != "p2p":
             hidden_states, hidden_states_scale = B.quantize_hidden(hidden_states)
-        if self.plumbing == "torch":
-            return self._forward_torch(routing_logits, routing_bias, hidden_states, hidden_states_scale,
-                                       routed_scaling_factor)
         # the library's entry points launch on the current device: make it the rows' device
         with torch.cuda.device(hidden_states.device):
-            if self.plumbing == "p2p":
+            if self.exchange == "p2p":
                 return self._forward_p2p(routing_logits, routing_bias, hidden_states, hidden_states_scale,
                                          routed_scaling_factor)
-            return self._forward_cuda(routing_logits, routing_bias, hidden_states, hidden_states_scale,
+            return self._forward_nccl(routing_logits, routing_bias, hidden_states, hidden_states_scale,
                                       routed_scaling_factor)
 
-    def _forward_cuda(self, routing_logits, routing_bias, hidden_states, hidden_states_scale, routed_scaling_factor):
+    def _forward_nccl(self, routing_logits, routing_bias, hidden_states, hidden_states_scale, routed_scaling_factor):
         from . import binding as B
-        idx, w = self.route_fn(routing_logits, routing_bias, routed_scaling_factor)
+        idx, w = B.route(routing_logits, routing_bias, routed_scaling_factor)
         send, send_counts, pos = B.ep_dispatch(idx, w, hidden_states, hidden_states_scale, self.world)
         recv_counts = _exchange_counts(send_counts, self.group)
         s_split = send_counts.tolist()
@@ -304,7 +226,7 @@ class ExpertParallelMoE:
             t_max = int(t.item())
             self._peer = PeerExchange(t_max * world, int(lib.kf_ep_max_send_rows(t_max, world)), world, rank,
                                       self.group, dev)
-        idx, w = self.route_fn(routing_logits, routing_bias, routed_scaling_factor)
+        idx, w = B.route(routing_logits, routing_bias, routed_scaling_factor)
         hid = hidden_states.contiguous()
         hs = hidden_states_scale.contiguous() if hidden_states_scale is not None else None
         if hs is None and hid.dtype != torch.bfloat16:
@@ -346,24 +268,3 @@ class ExpertParallelMoE:
                              self.w.gemm2_weights_scale, self.offset, pe.counts, rank, world, pe.peer_back)
         pe.barrier(stream)                      # every partial of this rank's rows is back
         return B.ep_combine(pe.back[:S], pos, world)
-
-    def _forward_torch(self, routing_logits, routing_bias, hidden_states, hidden_states_scale,
-                       routed_scaling_factor):
-        T = routing_logits.shape[0]
-        idx, w = self.route_fn(routing_logits, routing_bias, routed_scaling_factor)
-        plan = dispatch_plan(idx, w, self.world)
-        send = pack_rows(hidden_states, hidden_states_scale.contiguous(), plan)
-        recv_counts = _exchange_counts(plan.send_counts, self.group)
-        s_split = plan.send_counts.tolist()
-        r_split = recv_counts.tolist()
-        recv = torch.empty((sum(r_split), ROW_BYTES), dtype=torch.uint8, device=send.device)
-        dist.all_to_all_single(recv, send, output_split_sizes=r_split, input_split_sizes=s_split, group=self.group)
-        hid, sc, ids, ww = unpack_rows(recv)
-        self._last_ids = ids
-        part = self.experts_fn(ids, ww, hid, sc, self.w.gemm1_weights, self.w.gemm1_weights_scale,
-                               self.w.gemm2_weights, self.w.gemm2_weights_scale, self.offset,
-                               out_dtype=self.combine_dtype)
-        back = torch.empty((sum(s_split), H), dtype=part.dtype, device=part.device)
-        dist.all_to_all_single(back, part.contiguous(), output_split_sizes=s_split, input_split_sizes=r_split,
-                               group=self.group)
-        return combine(back, plan.pos) if T else torch.empty((0, H), dtype=torch.bfloat16, device=back.device)

@@ -15,9 +15,10 @@ its output), and the entry point ``kernelforge_b200/binding.py::kernel`` whose
 ten positional parameters are the reference's.
 
 The sources are exactly what the entry point needs: the Python binding and its
-nvcc build step, the CUDA sources and the C-ABI header.  On first call the
-binding compiles ``libkf_moe.so`` for sm_100a from them (``build.py``); it has
-no CPU fallback.  How the contest harness's own CUDA builder treats these
+build step, the CUDA sources, the PyTorch C++ extension over the C ABI and the
+C-ABI header.  On first call the binding compiles ``libkf_moe.so`` for sm_100a
+and the extension ``_kf_torch.so`` from them (``build.py``); it has no CPU
+fallback.  How the contest harness's own CUDA builder treats these
 sources is not known here (the harness is not available), so the JSON is
 checked by round-tripping it: unpacked into an empty directory, the sources
 build and the entry point imports.
@@ -42,7 +43,7 @@ def source_files() -> List[str]:
     """Repository-relative paths of every file the packed solution carries."""
     from . import build
     files = [os.path.join("kernelforge_b200", f) for f in PY_SOURCES]
-    files += [os.path.join("kernelforge_b200", "csrc", f) for f in build.SOURCES + build.HEADERS]
+    files += [os.path.join("kernelforge_b200", "csrc", f) for f in build.SOURCES + build.HEADERS + [build.EXT_SOURCE]]
     files.append(os.path.join("include", "kf_moe.h"))
     return files
 

@@ -29,7 +29,7 @@ def worker(rank, world, port, T, result_dir):
         E = 256 // world
         ti = S.token_inputs(T, seed=60 + rank, device=dev)
         shard = S.expert_bank(E, rank * E, seed=3, device=dev)
-        layer = ep.ExpertParallelMoE(shard, rank * E, E, combine_dtype=torch.float32, plumbing="cuda")
+        layer = ep.ExpertParallelMoE(shard, rank * E, E, combine_dtype=torch.float32, exchange="nccl")
         out = layer.forward(ti.routing_logits, ti.routing_bias, ti.hidden_states, ti.hidden_states_scale, 2.5)
         torch.cuda.synchronize(dev)
         res["status"] = B.read_status(dev)
@@ -46,8 +46,8 @@ def worker(rank, world, port, T, result_dir):
         res["ep_vs_single_maxdiff"] = float((out.float() - single.float()).abs().max())
         # the peer-to-peer exchange against the NCCL one (same kernels and combine order: bit-identical),
         # over two steps in a row (the barrier epochs advance and the buffers are reused)
-        nccl = ep.ExpertParallelMoE(shard, rank * E, E, plumbing="cuda")
-        p2p = ep.ExpertParallelMoE(shard, rank * E, E, plumbing="p2p")
+        nccl = ep.ExpertParallelMoE(shard, rank * E, E, exchange="nccl")
+        p2p = ep.ExpertParallelMoE(shard, rank * E, E, exchange="p2p")
         args = (ti.routing_logits, ti.routing_bias, ti.hidden_states, ti.hidden_states_scale, 2.5)
         o_nccl = nccl.forward(*args)
         o_p2p = [p2p.forward(*args) for _ in range(2)]
@@ -60,7 +60,7 @@ def worker(rank, world, port, T, result_dir):
         res["nccl_pairs"] = nccl.local_pairs()
         # uneven token counts (one rank empty in the second step): the receive and return areas are
         # sized from the count matrix every rank holds, and grow together when a step needs more
-        uneven = ep.ExpertParallelMoE(shard, rank * E, E, plumbing="p2p")
+        uneven = ep.ExpertParallelMoE(shard, rank * E, E, exchange="p2p")
         res["uneven"] = []
         for step, Ts in enumerate(([64, 32], [700, 0])):
             tu = S.token_inputs(Ts[rank], seed=90 + 10 * step + rank, device=dev)

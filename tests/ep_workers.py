@@ -11,9 +11,9 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-from kernelforge_b200 import ep  # noqa: E402
 from kernelforge_b200 import synthetic as S  # noqa: E402
 from oracle import moe_oracle as O  # noqa: E402
+from tests import ep_reference as R  # noqa: E402
 
 
 def oracle_route(logits, bias, rsf):
@@ -52,9 +52,8 @@ def worker(rank, world, port, T_per_rank, combine, mode, result_dir):
         E = 256 // world
         T = T_per_rank[rank]
         ti = tokens_for(rank, T)
-        layer = ep.ExpertParallelMoE(dummy_bank(E), rank * E, E,
-                                     combine_dtype=torch.float32 if combine == "f32" else torch.bfloat16,
-                                     experts_fn=linear_experts, route_fn=oracle_route, plumbing="torch")
+        layer = R.TorchExchangeMoE(dummy_bank(E), rank * E, E, route_fn=oracle_route, experts_fn=linear_experts,
+                                   combine_dtype=torch.float32 if combine == "f32" else torch.bfloat16)
         if mode == "drop" and rank == world - 1:
             res["dropped"] = True      # leaves before its first collective
             torch.save(res, os.path.join(result_dir, f"r{rank}.pt"))
@@ -65,7 +64,7 @@ def worker(rank, world, port, T_per_rank, combine, mode, result_dir):
                              None, 0, out_dtype=torch.float32)
         res["out"] = out
         res["ref"] = ref
-        res["sent"] = ep.dispatch_plan(idx, w, world).send_counts
+        res["sent"] = R.dispatch_plan(idx, w, world).send_counts
         dist.barrier()
         dist.destroy_process_group()
     except Exception as exc:  # reported to the test, which decides whether it was expected

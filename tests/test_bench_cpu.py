@@ -18,6 +18,9 @@ def _check_reference_line(d, n_gpus):
     assert d["unit"] == "tokens/s" and d["higher_is_better"] is True and d["value"] > 0
     assert d["metric"].startswith("MoE layer tokens/s")
     assert d["config"]["workload"] == "ep_layer_T8192_per_gpu_256_experts"
+    assert d["config"]["local_experts_per_gpu"] == 256 // n_gpus
+    # measured, not extrapolated: the steps' time is the measured slices' time
+    assert abs(d["ms_per_step"] * d["steps"] / 1e3 - d["tokens_per_step"] * d["steps"] / d["value"]) < 1e-6 * d["ms_per_step"]
     cb = d["cpu_baseline"]
     assert cb["kind"] == "port" and cb["value"] == d["value"] and cb["cores"] >= 1 and cb["sample"]
     assert d["e2e"] == {"value": d["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
@@ -145,11 +148,34 @@ def test_clock_sampler_without_nvidia_smi_reports_unsampled():
 
 
 def test_cpu_baseline_object_of_the_bench_line():
-    """The main arm's cpu_baseline on a decode-sized workload (16 tokens, 32 local experts), and its
-    error report when the sample cannot be built."""
+    """The main arm's cpu_baseline on a decode-sized workload (16 tokens, 32 local experts): the whole
+    layer timed as its slices, and the error report when the layer cannot be built."""
     b = _bench()
-    c = b.measure_cpu_baseline(16, 32, 0, repeats=1)
-    assert c["kind"] == "port" and c["value"] > 0 and c["cores"] >= 1 and "active experts" in c["sample"]
+    c = b.measure_cpu_baseline(16, 32, 0, parts=4)
+    assert c["kind"] == "port" and c["value"] > 0 and c["cores"] >= 1 and "active" in c["sample"]
     for args in ((16, 32, 300), (-1, 32, 0)):   # experts past 256 / no inputs: reported, not raised
-        err = b.measure_cpu_baseline(*args, repeats=1)
+        err = b.measure_cpu_baseline(*args, parts=4)
         assert err["value"] is None and err["error"]
+
+
+def test_cpu_slices_partition_the_layer():
+    """The reference arm's slices cover every token's routing, every output row and every active
+    expert exactly once per round of `parts` slices."""
+    b = _bench()
+    lay = b.CpuReferenceLayer(40, 32, 0, parts=4, pool=1)
+    seen_experts = []
+    for j in range(4):
+        seen_experts += list(range(j, 32, 4))
+        lay.run_part(j)
+    assert sorted(seen_experts) == list(range(32))
+    rows = [range(j * 40 // 4, (j + 1) * 40 // 4) for j in range(4)]
+    assert sorted(r for rr in rows for r in rr) == list(range(40))
+
+
+def test_reference_and_own_arm_share_the_config():
+    import argparse
+    b = _bench()
+    for world in (1, 2, 8):
+        args = argparse.Namespace(workload="ep", tokens=None, ep_exchange="p2p", graph=False, zipf=False)
+        T, E, name = b.workload_shape(args, world)
+        assert b.line_config(name, T, E, world, args)["local_experts_per_gpu"] == 256 // world

@@ -8,6 +8,7 @@ import pytest
 import torch
 
 from kernelforge_b200 import ep
+from tests import ep_reference as R
 from tests.ep_workers import oracle_route, tokens_for, worker
 
 
@@ -38,7 +39,7 @@ def test_dispatch_plan_dedups_and_masks():
     ti = tokens_for(0, 64)
     idx, w = oracle_route(ti.routing_logits, ti.routing_bias, 2.5)
     for world in (2, 4, 8):
-        plan = ep.dispatch_plan(idx, w, world)
+        plan = R.dispatch_plan(idx, w, world)
         per = 256 // world
         dest = idx.long() // per
         for t in range(64):
@@ -57,10 +58,10 @@ def test_dispatch_plan_dedups_and_masks():
 def test_pack_unpack_roundtrip():
     ti = tokens_for(1, 10)
     idx, w = oracle_route(ti.routing_logits, ti.routing_bias, 2.5)
-    plan = ep.dispatch_plan(idx, w, 4)
-    rows = ep.pack_rows(ti.hidden_states, ti.hidden_states_scale, plan)
+    plan = R.dispatch_plan(idx, w, 4)
+    rows = R.pack_rows(ti.hidden_states, ti.hidden_states_scale, plan)
     assert rows.shape == (plan.send_token.numel(), ep.ROW_BYTES) and ep.ROW_BYTES % 16 == 0
-    hid, sc, ids, ww = ep.unpack_rows(rows)
+    hid, sc, ids, ww = R.unpack_rows(rows)
     assert torch.equal(hid.view(torch.uint8), ti.hidden_states.index_select(0, plan.send_token).view(torch.uint8))
     assert torch.equal(sc, ti.hidden_states_scale[:, plan.send_token])
     assert torch.equal(ids, plan.send_ids) and torch.equal(ww, plan.send_w)
@@ -111,7 +112,7 @@ def test_peer_status_errors_are_decoded_and_sticky():
     assert "barrier" in ep.peer_status_error(ep.STATUS_TIMEOUT_PEER)
     assert "overflowed" in ep.peer_status_error(ep.STATUS_SLOT_OVERFLOW)
     m = object.__new__(ep.ExpertParallelMoE)
-    m.plumbing = "p2p"
+    m.exchange = "p2p"
     m._peer = None
     m.check()                                           # before the first step: nothing to check
     m._peer = SimpleNamespace(status=torch.zeros(1, dtype=torch.int32))
@@ -120,5 +121,5 @@ def test_peer_status_errors_are_decoded_and_sticky():
     for _ in range(2):
         with pytest.raises(RuntimeError, match="0x20"):
             m.check()
-    m.plumbing = "cuda"
-    m.check()                                           # NCCL plumbing: its collectives raise instead
+    m.exchange = "nccl"
+    m.check()                                           # NCCL exchange: its collectives raise instead

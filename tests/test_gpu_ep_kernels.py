@@ -1,12 +1,13 @@
-"""Expert-parallel CUDA plumbing on one GPU (ranks emulated): dispatch packing,
+"""Expert-parallel CUDA kernels on one GPU (ranks emulated): dispatch packing,
 the packed-row experts entry point and the combine, each bit-exact against the
-tensor-op restatement in kernelforge_b200.ep."""
+tensor-op restatement in tests/ep_reference.py."""
 import pytest
 import torch
 
 from kernelforge_b200 import binding as B
 from kernelforge_b200 import ep
 from kernelforge_b200 import synthetic as S
+from tests import ep_reference as R
 from tests.helpers import gpu_available, gpu_bank, to_cuda
 
 pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not gpu_available(), reason="needs a B200")]
@@ -18,8 +19,8 @@ def test_dispatch_matches_restatement(world, T):
     ti = to_cuda(S.token_inputs(T, seed=70 + T))
     idx, w = B.route(ti.routing_logits, ti.routing_bias, 2.5)
     send, counts, pos = B.ep_dispatch(idx, w, ti.hidden_states, ti.hidden_states_scale, world)
-    plan = ep.dispatch_plan(idx, w, world)
-    ref_rows = ep.pack_rows(ti.hidden_states, ti.hidden_states_scale, plan)
+    plan = R.dispatch_plan(idx, w, world)
+    ref_rows = R.pack_rows(ti.hidden_states, ti.hidden_states_scale, plan)
     torch.cuda.synchronize()
     assert torch.equal(counts.cpu(), plan.send_counts.cpu())
     assert torch.equal(pos.long(), plan.pos)
@@ -39,7 +40,7 @@ def test_experts_packed_matches_unpacked():
     bank = gpu_bank(E, r * E, seed=9)
     out_p = B.experts_packed(rows, bank.gemm1_weights, bank.gemm1_weights_scale, bank.gemm2_weights,
                              bank.gemm2_weights_scale, r * E)
-    hid, sc, ids, ww = ep.unpack_rows(rows)
+    hid, sc, ids, ww = R.unpack_rows(rows)
     out_u = B.experts(ids, ww, hid, sc, bank.gemm1_weights, bank.gemm1_weights_scale, bank.gemm2_weights,
                       bank.gemm2_weights_scale, r * E)
     torch.cuda.synchronize()
@@ -56,7 +57,7 @@ def test_combine_matches_restatement(dtype):
     n = int(counts.sum())
     back = torch.randn(n, 7168, generator=torch.Generator(device="cuda").manual_seed(3), device="cuda").to(dtype)
     out = B.ep_combine(back, pos, world)
-    ref = ep.combine(back, pos.long())
+    ref = R.combine(back, pos.long())
     torch.cuda.synchronize()
     assert torch.equal(out, ref)
 

@@ -95,8 +95,12 @@ def test_every_device_entry_point_goes_through_the_device_guard():
     direct = [n for n in re.findall(r"(?:_load\(\)|lib)\.(kf_\w+)\(", src) if n not in host_only]
     assert not direct, f"called without _call: {direct}"
     routed = re.findall(r"_call\(\s*[\w.]+,\s*(?:_load\(\)|lib)\.(kf_\w+),", src)
-    assert {"kf_moe_forward", "kf_moe_route", "kf_moe_experts", "kf_moe_experts_packed", "kf_moe_experts_packed_p2p",
+    assert {"kf_moe_route", "kf_moe_experts", "kf_moe_experts_packed", "kf_moe_experts_packed_p2p",
             "kf_ep_dispatch", "kf_ep_combine", "kf_quantize_hidden", "kf_moe_read_status"} <= set(routed)
+    # kernel() goes through the torch extension, which makes the tensors' device current the same way
+    ext = open(os.path.join(ROOT, "kernelforge_b200", "csrc", "kf_torch_ext.cpp")).read()
+    body = ext[ext.index("at::Tensor kernel("):]
+    assert body.index("c10::cuda::CUDAGuard guard(dev)") < body.index("kf_moe_forward(")
 
 
 def test_release_workspaces_empties_the_caches():
@@ -152,3 +156,17 @@ def test_noalloc_static_scratch_covers_its_limits():
     scratch = int(size.group(1)) << int(size.group(2))
     lib = B.library()
     assert all(lib.kf_moe_workspace_bytes(t, e) <= scratch for t in (1, max_t) for e in (1, max_e))
+
+
+def test_torch_extension_binds_the_c_abi():
+    """The PyTorch C++ extension loads beside libkf_moe.so, exposes the operator and refuses CPU tensors
+    itself (no GPU needed)."""
+    from kernelforge_b200 import synthetic as S
+    ext = B.extension()
+    assert callable(ext.kernel) and callable(ext.read_status) and callable(ext.release_workspaces)
+    ti = S.token_inputs(2, seed=0)
+    wb = S.expert_bank(1, 0, only=[])
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        ext.kernel(ti.routing_logits, ti.routing_bias, ti.hidden_states, ti.hidden_states_scale, wb.gemm1_weights,
+                   wb.gemm1_weights_scale, wb.gemm2_weights, wb.gemm2_weights_scale, 0, 2.5)
+    ext.release_workspaces()

@@ -50,11 +50,13 @@ def test_unpack_rejects_escaping_paths(tmp_path):
 
 @pytest.mark.skipif(not os.path.exists(os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")), reason="needs nvcc")
 def test_unpacked_sources_build_and_import(tmp_path):
-    """The sources alone rebuild libkf_moe.so for sm_100a and the entry point imports (no GPU needed)."""
+    """The sources alone rebuild libkf_moe.so for sm_100a and its torch extension, and the entry point
+    imports (no GPU needed)."""
     P.unpack(P.solution_dict(), str(tmp_path))
     code = ("import sys; sys.path.insert(0, '.'); from kernelforge_b200 import build; "
-            "build.build(force=True); import kernelforge_b200.binding as b; "
-            "lib = b.library(); print(callable(b.kernel), lib.kf_moe_launches_per_forward())")
+            "build.build(force=True); build.build_ext(force=True); import kernelforge_b200.binding as b; "
+            "lib = b.library(); ext = b.extension(); "
+            "print(callable(b.kernel) and callable(ext.kernel), lib.kf_moe_launches_per_forward())")
     r = subprocess.run([sys.executable, "-c", code], cwd=tmp_path, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stderr[-2000:]
     assert r.stdout.split()[-2:] == ["True", "7"]
