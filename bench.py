@@ -3,7 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kernelforge|reference]
                     [--workload ep|prefill|decode] [--tokens T] [--zipf] [--graph]
-                    [--ep-exchange p2p|nccl] [--no-cpu-baseline]
+                    [--ep-exchange p2p|nccl] [--no-cpu-baseline] [--no-extra]
 
 Default workload ("ep", the layer of config 3 of the headline metric): 8192
 tokens per GPU, all 256 experts sharded 256/N per GPU (N=1: all 256 on one GPU),
@@ -17,16 +17,25 @@ GPU's 8192 tokens; per-GPU work is fixed as N grows (weak scaling).
 Prints ONE JSON line (rank 0).  Metric: tokens/s of the whole job (all GPUs).
 Inputs are synthetic (seeded N(0,1) logits / activations, N(0,0.02) weights,
 generated on the GPU); the weights (11.3 GB) are far larger than L2, so every
-step streams them from HBM (no L2 flush needed).
+step streams them from HBM (no L2 flush needed).  After the timed steps the line
+also carries a sampled parity check of the step's output against the fp32
+reference ("parity"), and at N = 1 the single-GPU configurations of the metric:
+the decode sweep (config 1: p50 microseconds and HBM fraction, L2 flushed before
+every call), prefill (config 2: FP8 fraction of GEMM1) and the Zipf-skewed layer
+(config 4) ("single_gpu_configs").
 
 --impl reference times the reference algorithm's CPU path (the oracle port of
-solution/triton/kernel.py::kernel's PyTorch loop) on this host's cores: per step,
-all tokens routed and the expert loop run on 8 of the active experts, scaled to
-all of them (CpuOracleSample).
+solution/triton/kernel.py::kernel's PyTorch loop) on this host's cores.  The
+layer is cut into 32 equal slices -- slice j routes tokens [jT/32, (j+1)T/32),
+runs the expert loop for the local experts e = j (mod 32) with all of their
+pairs, and zeroes and casts its share of the output rows -- so 32 consecutive
+slices do exactly the work of one layer call.  Each step times one slice (the
+next in turn); value = tokens of layer work per measured second.
 """
 from __future__ import annotations
 
 import argparse
+import hashlib
 import json
 import os
 import re
@@ -48,7 +57,11 @@ W13_BYTES_PER_EXPERT = 2 * I * H                   # 29,360,128 (e4m3)
 W2_BYTES_PER_EXPERT = H * I                        # 14,680,064
 W13_SCALE_BYTES = (2 * I // 128) * (H // 128) * 4
 W2_SCALE_BYTES = (H // 128) * (I // 128) * 4
+EXPERT_BYTES = W13_BYTES_PER_EXPERT + W2_BYTES_PER_EXPERT + W13_SCALE_BYTES + W2_SCALE_BYTES
+TOKEN_IN_BYTES = H + (H // 128) * 4 + E_GLOBAL * 4    # fp8 row, its scales, its routing logits
+TOKEN_OUT_BYTES = H * 2                               # bf16 output row
 METRIC = "MoE layer tokens/s (FP8 block-scale DeepSeek-V3 layer, T=8192 tokens per GPU, 256 experts EP-sharded)"
+CPU_PARTS = 32
 
 
 def parse():
@@ -60,6 +73,7 @@ def parse():
     p.add_argument("--workload", default="ep", choices=["ep", "prefill", "decode"])
     p.add_argument("--tokens", type=int, default=None)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-extra", action="store_true", help="skip the single-GPU configurations (N = 1)")
     p.add_argument("--graph", action="store_true", help="replay the layer as a CUDA graph (1 GPU)")
     p.add_argument("--zipf", action="store_true",
                    help="config 4: routing bias skewing expert popularity to Zipf(1.2) over a seeded permutation")
@@ -76,6 +90,14 @@ def load_peaks():
         return {"hbm_gbs": d["hbm_gbs"], "bf16": d["bf16_tflops"], "bf16_sustained": d["bf16_tflops_sustained"],
                 "source": "measured"}
     return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+def fp8_peak(peaks) -> dict:
+    """FP8 dense peak for a kernel timed in short steps: 2 x the burst bf16 cuBLAS figure.  The pool
+    measures no FP8 GEMM; the factor 2 is the nominal fp8/bf16 ratio (4.5 / 2.25 PFLOP/s), assumed."""
+    return {"peak": 2.0 * peaks["bf16"],
+            "peak_note": f"FP8 dense taken as 2 x the {peaks['source']} burst cuBLAS bf16 figure "
+                         f"({peaks['bf16']} TFLOP/s); the factor 2 is assumed (no FP8 GEMM is measured)"}
 
 
 CLOCK_FIELDS = ("index,uuid,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
@@ -235,106 +257,275 @@ def workload_shape(args, world):
 
 
 # ---------------------------------------------------------------- CPU baseline --
-class CpuOracleSample:
-    """A bounded sample of the workload for the reference algorithm's CPU path, timed so that it
-    scales to the whole layer.
+class CpuReferenceLayer:
+    """The reference algorithm's CPU layer on the bench's workload, cut into equal timed slices.
 
-    The reference's CPU layer (``solution/triton/kernel.py:1927-1950``, restated in
-    ``oracle/moe_oracle.py``) loops over the active local experts independently: each iteration
-    dequantises one expert's weights and its rows and runs that expert's two GEMMs, so dequantising
-    weights is paid once per expert and amortised over its pairs.  A sample of a few tokens would
-    pay it for a handful of pairs and understate the path's throughput by orders of magnitude.
-    This sample keeps the workload's amortisation.  It routes all T tokens, then runs the loop for
-    k of the active experts (at the midpoints of k quantiles of the per-expert pair counts) with all
-    of their pairs, and scales that loop time by active/k.  The per-call fixed work (zeroing the fp32 accumulator, the bf16 cast) is timed as a
-    call with no local pair and counted once.  The expert weights are generated once, outside the
-    timing.
+    The reference's CPU path (``solution/triton/kernel.py:1842-1950``: routing, ``_sort_tokens``,
+    then a loop over the active local experts that dequantises each expert's weights and rows and
+    runs its two GEMMs and the weighted ``index_add_``), restated in ``oracle/moe_oracle.py``, is
+    cut into ``parts`` slices: slice j routes tokens ``[jT/parts, (j+1)T/parts)``, zeroes and
+    casts to bf16 that share of the output rows, and runs the expert loop for the local experts
+    e = j (mod parts) with all of their pairs (their pair lists taken from the routing of every
+    token, made once outside the timing).  The ``parts`` slices together do exactly the work of
+    one layer call; every slice is timed on its own.  The expert weights come from a pool of
+    ``pool`` generated experts (expert e uses pool entry e mod pool): their values do not change
+    the cost of the dense fp32 arithmetic, and generating all 256 would take minutes.  The slices
+    time the work; their accumulated output is not the layer's (each slice casts its rows before
+    later slices add into them).
     """
 
-    def __init__(self, T: int, num_local: int, offset: int = 0, k: int = 8, seed: int = 1000):
+    def __init__(self, T: int, num_local: int, offset: int = 0, parts: int = CPU_PARTS, pool: int = 8,
+                 seed: int = 1000, routing_bias=None):
         from kernelforge_b200 import synthetic as S
         from oracle import moe_oracle as O
+        if T <= 0 or num_local < 1 or offset < 0 or offset + num_local > E_GLOBAL:
+            raise ValueError(f"no CPU layer for T={T}, experts [{offset}, {offset + num_local})")
         torch.set_num_threads(os.cpu_count() or 1)
-        self.O, self.T = O, T
-        self.ti = S.token_inputs(T, seed=seed)
-        idx, _ = O.route(self.ti.routing_logits, self.ti.routing_bias, 2.5)
-        counts = torch.bincount(idx.flatten().long(), minlength=E_GLOBAL)
-        self.active = [e for e in range(offset, offset + num_local) if counts[e] > 0]
-        # experts at the midpoints of k equal quantiles of the pair counts: the sample's pairs per
-        # expert track the population's, so both the per-expert and the per-pair work scale by active/k
-        by_count = sorted(self.active, key=lambda e: (int(counts[e]), e))
-        k = min(k, len(self.active))
-        self.sample = sorted(by_count[int((i + 0.5) * len(by_count) / k)] for i in range(k))
-        self.total_pairs = int(sum(int(counts[e]) for e in self.active))
-        # with no local pair the loop is empty and never reads the (placeholder) weights
-        banks = [S.expert_weights(g, seed=0) for g in (self.sample or [offset])]
-        self.w = [torch.stack([b[i] for b in banks]) for i in range(4)]
-        self.lut = torch.full((E_GLOBAL,), -1, dtype=torch.int64)
-        if self.sample:
-            self.lut[torch.tensor(self.sample)] = torch.arange(len(self.sample))
-        self.pairs = int((self.lut[idx] >= 0).sum())
+        self.O, self.T, self.E, self.offset, self.parts = O, T, num_local, offset, parts
+        self.ti = S.token_inputs(T, seed=seed, routing_bias=routing_bias)
+        self.idx, self.w = O.route(self.ti.routing_logits, self.ti.routing_bias, 2.5)
+        self.loc = self.idx - offset
+        self.pool = [S.expert_weights(offset + e, seed=0) for e in range(min(pool, num_local))]
+        self.acc = torch.zeros(T, H, dtype=torch.float32)
+        self.out = torch.empty(T, H, dtype=torch.bfloat16)
+        self.active = int(torch.unique(self.loc[(self.loc >= 0) & (self.loc < num_local)]).numel())
 
-    def time_once(self) -> float:
-        """Estimated seconds of the whole layer on this host (one timed sample)."""
+    def run_part(self, j: int) -> float:
+        """Seconds of slice j."""
         O, ti = self.O, self.ti
-        t0 = time.perf_counter()
-        idx, w = O.route(ti.routing_logits, ti.routing_bias, 2.5)
-        cidx = self.lut[idx]
-        wsel = torch.gather(w, 1, idx)
-        t1 = time.perf_counter()
-        O.moe_experts(cidx, wsel, ti.hidden_states, ti.hidden_states_scale, *self.w, 0).to(torch.bfloat16)
-        t2 = time.perf_counter()
-        O.moe_experts(torch.full_like(cidx, -1), wsel, ti.hidden_states, ti.hidden_states_scale, *self.w,
-                      0).to(torch.bfloat16)
-        t3 = time.perf_counter()
-        fixed = t3 - t2
-        loop = max(0.0, (t2 - t1) - fixed)
-        scale = len(self.active) / len(self.sample) if self.sample else 0.0
-        return (t1 - t0) + fixed + loop * scale
+        t0 = j * self.T // self.parts
+        t1 = (j + 1) * self.T // self.parts
+        s = time.perf_counter()
+        O.route(ti.routing_logits[t0:t1], ti.routing_bias, 2.5)
+        self.acc[t0:t1].zero_()
+        for e in range(j, self.E, self.parts):
+            tok = torch.nonzero((self.loc == e).any(dim=1)).flatten()      # token order (stable)
+            if tok.numel() == 0:
+                continue
+            rows = O.dequant_hidden_rows(ti.hidden_states, ti.hidden_states_scale, tok)
+            y = O.expert_forward(rows, *self.pool[e % len(self.pool)])
+            rw = self.w[tok, self.offset + e]
+            self.acc.index_add_(0, tok, y * rw.unsqueeze(1))
+        self.out[t0:t1] = self.acc[t0:t1].to(torch.bfloat16)
+        return time.perf_counter() - s
 
-    def describe(self, est_s: float) -> str:
-        return (f"all {self.T} tokens routed; the expert loop timed on {len(self.sample)} of the "
-                f"{len(self.active)} active experts ({self.pairs} of {self.total_pairs} pairs) and scaled by "
-                f"{len(self.active)}/{max(1, len(self.sample))}; estimated layer {est_s:.1f} s (PyTorch CPU, "
-                f"reference algorithm restated in oracle/moe_oracle.py)")
+    def describe(self) -> str:
+        return (f"reference CPU layer (oracle/moe_oracle.py restatement of kernel.py:1842-1950, PyTorch fp32, "
+                f"{torch.get_num_threads()} threads) on T={self.T} tokens and {self.E} local experts "
+                f"({self.active} active), cut into {self.parts} slices that together do one layer's work: "
+                f"slice j routes 1/{self.parts} of the tokens, casts 1/{self.parts} of the output rows and runs "
+                f"the expert loop of the experts e = j (mod {self.parts}); weights from a pool of "
+                f"{len(self.pool)} generated experts")
 
 
-def measure_cpu_baseline(T: int, num_local: int, offset: int, repeats: int = 3) -> dict:
-    """The ``cpu_baseline`` object of the bench line: the median of `repeats` CpuOracleSample
-    estimates after one warm-up.  A failure is reported inside the object (it must not cost the
-    measured line it rides on)."""
+def zipf_cpu_bias():
+    from kernelforge_b200 import synthetic as S
+    return S.zipf_bias(seed=0)
+
+
+def measure_cpu_baseline(T: int, num_local: int, offset: int, parts: int = CPU_PARTS, routing_bias=None) -> dict:
+    """The ``cpu_baseline`` object of the bench line: the whole layer once, every slice timed (about
+    10-30 s of CPU work at the bench's workload).  A failure is reported inside the object (it must
+    not cost the measured line it rides on)."""
     try:
-        smp = CpuOracleSample(T, num_local, offset)
-        smp.time_once()
-        est = statistics.median(smp.time_once() for _ in range(repeats))
-        return {"value": T / est, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
-                "sample": f"median of {repeats}: " + smp.describe(est)}
+        lay = CpuReferenceLayer(T, num_local, offset, parts=parts, routing_bias=routing_bias)
+        lay.run_part(0)                                 # warm-up (allocator, thread pool)
+        total = sum(lay.run_part(j) for j in range(parts))
+        return {"value": T / total, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+                "sample": f"the whole layer once ({parts} slices, {total:.1f} s measured): " + lay.describe()}
     except Exception as exc:  # noqa: BLE001 -- reported in the line, not swallowed
         return {"value": None, "unit": "tokens/s", "error": f"{type(exc).__name__}: {exc}"}
+
+
+def line_config(name, T, E, world, args, pairs=None):
+    """The ``config`` object, the same in both arms."""
+    return {"workload": name, "tokens_per_gpu": T, "local_experts_per_gpu": E, "global_experts": E_GLOBAL,
+            "hidden": H, "intermediate": I, "top_k": 8, "parallelism": f"ep{world}",
+            "ep_exchange": args.ep_exchange if world > 1 else None,
+            "l2": "inputs larger than L2 (weights stream from HBM)", "cuda_graph": bool(args.graph and world == 1)}
 
 
 def run_reference(args, world, rank):
     if rank != 0:
         return
-    T, E, name = workload_shape(args, 1)
-    smp = CpuOracleSample(T, E)
+    # the same per-GPU workload and config as this N's own arm; the CPU layer routes the GPU's T
+    # tokens over all the experts they reach (all 256 for the expert-parallel layer: the per-token
+    # work of the whole job)
+    T, E, name = workload_shape(args, args.gpus)
+    if args.zipf:
+        name += "_zipf1.2"
+    lay = CpuReferenceLayer(T, E_GLOBAL if args.workload == "ep" else E,
+                            routing_bias=zipf_cpu_bias() if args.zipf else None)
     cores = torch.get_num_threads()
+    part = 0
     for _ in range(args.warmup):
-        smp.time_once()
-    ests = [smp.time_once() for _ in range(args.steps)]
-    t_all = sum(ests)
-    value = T * args.steps / t_all
+        lay.run_part(part % lay.parts)
+        part += 1
+    times = []
+    for _ in range(args.steps):
+        times.append(lay.run_part(part % lay.parts))
+        part += 1
+    total = sum(times)
+    value = (T / lay.parts) * args.steps / total
+    sample = (f"each step is one slice (1/{lay.parts} of the layer's work, the next slice in turn), timed: "
+              + lay.describe())
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t_all / args.steps,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": name, "tokens_per_gpu": T, "experts": E_GLOBAL,
-                   "sample": "per step: " + smp.describe(statistics.median(ests))},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": smp.describe(statistics.median(ests))},
+        "config": line_config(name, T, E, args.gpus, args),
+        "tokens_per_step": T / lay.parts,
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------- parity --
+def sampled_parity(out, ti, idx, w, bank_fn, offset_of, n_sample: int = 256, seed: int = 5) -> dict:
+    """The step's output on a seeded sample of tokens against the fp32 reference (the oracle's
+    expert math on this GPU, ``oracle/moe_oracle.py``), with the layer's acceptance test.
+
+    ``idx``/``w``: the step's routing of these tokens (int32 ids, weights [T, 8]), checked for
+    every token against the oracle's routing on the CPU; ``bank_fn(global_ids)`` returns the
+    weights of those experts stacked in the given (ascending) order."""
+    from oracle import moe_oracle as O
+    T = int(out.shape[0])
+    ref_idx, _ = O.route(ti.routing_logits.float().cpu(), ti.routing_bias.cpu(), 2.5)
+    routing_exact = bool(torch.equal(idx.long().cpu().sort(dim=1).values, ref_idx.sort(dim=1).values))
+    g = torch.Generator().manual_seed(seed)
+    sel = torch.randperm(T, generator=g)[:min(T, n_sample)].sort().values.to(out.device)
+    sidx = idx[sel].long()
+    experts = sorted(set(sidx.flatten().tolist()))
+    wb = bank_fn(experts)
+    remap = torch.full((E_GLOBAL,), -1, dtype=torch.long, device=out.device)
+    remap[torch.tensor(experts, device=out.device)] = torch.arange(len(experts), device=out.device)
+    ref = O.moe_experts(remap[sidx].to(torch.int32), w[sel], ti.hidden_states[sel], ti.hidden_states_scale[:, sel],
+                        *wb, 0).to(torch.bfloat16)
+    res = O.check_tolerance(out[sel], ref)
+    return {"ok": bool(res["ok"] and routing_exact), "routing_exact_all_tokens": routing_exact,
+            "tokens_checked": int(sel.numel()), "experts_checked": len(experts),
+            "max_abs_err": res["max_abs_err"], "max_abs_ref": res["max_abs_ref"], "frac_within": res["frac_within"],
+            "tolerance": "max|err| <= 1e-2 max|ref|, >= 99.9% within 1e-2 + 2e-2 |ref|; routing sets exact"}
+
+
+# ------------------------------------------------- single-GPU configurations --
+def time_calls(fn, n: int, warmup: int, flush=None):
+    """Per-call device milliseconds (CUDA events on the current stream), sorted; with ``flush`` (a
+    buffer larger than L2) it is rewritten before every call, outside the timed events."""
+    stream = torch.cuda.current_stream()
+    for _ in range(warmup):
+        fn()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+    for a, b in evs:
+        if flush is not None:
+            flush.add_(1)
+        a.record(stream)
+        fn()
+        b.record(stream)
+    torch.cuda.synchronize()
+    return sorted(a.elapsed_time(b) for a, b in evs)
+
+
+def single_gpu_configs(B, S, dev, peaks, bank256) -> dict:
+    """Configs 1, 2 and 4 of the headline metric on this GPU, each timed and with its roofline."""
+    fp8 = fp8_peak(peaks)
+    res = {"peaks": {"hbm_gbs": peaks["hbm_gbs"], "fp8_tflops": fp8["peak"], "note": fp8["peak_note"]}}
+    wb32 = S.expert_bank(32, 0, seed=0, device=dev)
+    flush = torch.zeros(256 << 20, dtype=torch.uint8, device=dev)     # 256 MB > L2 (126 MB)
+
+    def layer(ti, wb):
+        return lambda: B.kernel(ti.routing_logits, ti.routing_bias, ti.hidden_states, ti.hidden_states_scale,
+                                wb.gemm1_weights, wb.gemm1_weights_scale, wb.gemm2_weights, wb.gemm2_weights_scale,
+                                0, 2.5)
+
+    def counts(ti, E):
+        idx, _ = B.route(ti.routing_logits, ti.routing_bias, 2.5)
+        loc = idx[(idx >= 0) & (idx < E)]
+        return int(loc.numel()), int(torch.unique(loc).numel())
+
+    def kernel_ms(fn, reps=10):
+        B.profile_begin()
+        for _ in range(reps):
+            fn()
+        torch.cuda.synchronize()
+        prof = B.profile_end()
+        return {k: v[0] / v[1] for k, v in prof.items() if v[1]}
+
+    # config 1: decode sweep, 32 local experts, weight-streaming bound
+    dec = {}
+    for T in (1, 2, 4, 8, 16, 32, 64):
+        ti = S.token_inputs(T, seed=300 + T, device=dev)
+        fn = layer(ti, wb32)
+        ms = time_calls(fn, 200, 10, flush=flush)
+        pairs, active = counts(ti, 32)
+        nbytes = active * EXPERT_BYTES + T * (TOKEN_IN_BYTES + TOKEN_OUT_BYTES) + 512
+        p50 = ms[len(ms) // 2]
+        km = kernel_ms(fn)
+        g1 = km.get("gemm1_swiglu")
+        g1_bytes = active * (W13_BYTES_PER_EXPERT + W13_SCALE_BYTES) + pairs * (H + (H // 128) * 4)
+        dec[f"T{T}"] = {"p50_us": 1e3 * p50, "p90_us": 1e3 * ms[int(len(ms) * 0.9)], "active_experts": active,
+                        "pairs": pairs, "layer_bytes": nbytes, "layer_hbm_gbs": nbytes / (p50 / 1e3) / 1e9,
+                        "layer_hbm_frac": nbytes / (p50 / 1e3) / 1e9 / peaks["hbm_gbs"],
+                        "gemm1_hbm_frac": (g1_bytes / (g1 / 1e3) / 1e9 / peaks["hbm_gbs"]) if g1 else None,
+                        "kernel_us": {k: 1e3 * v for k, v in km.items()}}
+    res["config1_decode"] = {"local_experts": 32, "l2": "256 MB buffer rewritten before every timed call",
+                             "calls": 200, "bytes": "active experts' W13+W2+scales + token rows in and out",
+                             "sweep": dec}
+
+    # config 2: prefill, 32 local experts, uniform routing
+    pre = {}
+    for T in (4096, 16384):
+        ti = S.token_inputs(T, seed=400 + T, device=dev)
+        fn = layer(ti, wb32)
+        ms = time_calls(fn, 20, 3)
+        pairs, active = counts(ti, 32)
+        p50 = ms[len(ms) // 2]
+        km = kernel_ms(fn, 5)
+        g1 = km["gemm1_swiglu"]
+        pre[f"T{T}"] = {"p50_ms": p50, "tokens_per_s": T / (p50 / 1e3), "pairs": pairs,
+                        "layer_tflops": FLOP_PER_PAIR * pairs / (p50 / 1e3) / 1e12,
+                        "layer_fp8_frac": FLOP_PER_PAIR * pairs / (p50 / 1e3) / 1e12 / fp8["peak"],
+                        "gemm1_tflops": GEMM1_FLOP_PER_PAIR * pairs / (g1 / 1e3) / 1e12,
+                        "gemm1_fp8_frac": GEMM1_FLOP_PER_PAIR * pairs / (g1 / 1e3) / 1e12 / fp8["peak"],
+                        "kernel_ms": km}
+    res["config2_prefill"] = {"local_experts": 32, "sweep": pre}
+
+    # config 4: Zipf(1.2)-skewed routing over all 256 experts on this GPU
+    if bank256 is not None:
+        zb = S.zipf_bias(seed=0).to(dev)
+        zz = {}
+        for T in (128, 1024, 4096, 16384):
+            ti = S.token_inputs(T, seed=500 + T, device=dev, routing_bias=zb)
+            fn = layer(ti, bank256)
+            ms = time_calls(fn, 10 if T >= 4096 else 30, 3)
+            pairs, active = counts(ti, 256)
+            p50 = ms[len(ms) // 2]
+            km = kernel_ms(fn, 3)
+            g1 = km["gemm1_swiglu"]
+            zz[f"T{T}"] = {"p50_ms": p50, "tokens_per_s": T / (p50 / 1e3), "pairs": pairs, "active_experts": active,
+                           "layer_hbm_frac": (active * EXPERT_BYTES / (p50 / 1e3) / 1e9) / peaks["hbm_gbs"],
+                           "gemm1_fp8_frac": GEMM1_FLOP_PER_PAIR * pairs / (g1 / 1e3) / 1e12 / fp8["peak"],
+                           "kernel_ms": km}
+        res["config4_zipf_256_experts"] = {"sweep": zz}
+    del wb32, flush
+    return res
+
+
+# DRAM bytes per GEMM1 launch from ncu captures (dram__bytes_read.sum + dram__bytes_write.sum), valid
+# only for the kernel source they were captured on: the line reports null once the source changes.
+TRAFFIC = {}
+
+
+def gemm1_traffic(name: str):
+    rec = TRAFFIC.get(name)
+    if rec is None:
+        return None, "no ncu capture of this workload"
+    with open(os.path.join(ROOT, "kernelforge_b200", "csrc", "kf_grouped_gemm.cu"), "rb") as f:
+        sha = hashlib.sha256(f.read()).hexdigest()[:16]
+    if sha != rec["source_sha16"]:
+        return None, "the GEMM kernels changed since the ncu capture"
+    return rec["bytes"], rec["note"]
 
 
 # ------------------------------------------------------------------- our arm --
@@ -362,9 +553,10 @@ def main():
     wb = S.expert_bank(E, offset, seed=0, device=dev)
     torch.cuda.synchronize(dev)
 
+    layer = None
     if world > 1:
         from kernelforge_b200 import ep
-        layer = ep.ExpertParallelMoE(wb, offset, E, plumbing="p2p" if args.ep_exchange == "p2p" else "cuda")
+        layer = ep.ExpertParallelMoE(wb, offset, E, exchange=args.ep_exchange)
 
         def step(logits, bias, hid, hs):
             return layer.forward(logits, bias, hid, hs, 2.5)
@@ -433,12 +625,11 @@ def main():
     ms_per_step = ms / args.steps
     value = world * T * args.steps / (ms / 1e3)
 
-    # End to end through the public API: every step copies its inputs from pinned
-    # host memory and its bf16 result back to pinned host memory.  As in a serving
+    # End to end through the public API: every step copies its inputs from pinned host
+    # memory and its bf16 result back to pinned host memory.  As in a serving
     # loop, the copies run on their own streams and overlap the neighbouring
     # steps' kernels: step k+1's inputs go up and step k-1's result comes down
     # while step k computes (two device input sets, two host output buffers).
-    e2e = None
     h_in = [tuple(t.cpu().pin_memory() for t in (ti.routing_logits, ti.routing_bias, ti.hidden_states,
                                                   ti.hidden_states_scale)) for _ in range(2)]
     h_out = [torch.empty((T, H), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
@@ -509,10 +700,35 @@ def main():
         err = ep.peer_status_error(int(st.item()))
         if err:
             raise RuntimeError(err)
+    else:
+        B.check(dev)        # device status of the timed calls (raises on a set bit)
+
+    # parity of one more step (all ranks run it: the exchange is collective), checked on rank 0
+    out = profiled_step(ti.routing_logits, ti.routing_bias, ti.hidden_states, ti.hidden_states_scale)
+    torch.cuda.synchronize(dev)
+    parity = None
+    if rank == 0:
+        ridx, rw = B.route(ti.routing_logits, ti.routing_bias, 2.5)
+        if world == 1:
+            def bank_fn(experts):
+                sel = torch.tensor(experts, device=dev) - offset
+                return (wb.gemm1_weights[sel], wb.gemm1_weights_scale[sel], wb.gemm2_weights[sel],
+                        wb.gemm2_weights_scale[sel])
+        else:
+            def bank_fn(experts):           # every rank's experts, generated here by global id
+                ws = [S.expert_weights(g, seed=0, device=dev) for g in experts]
+                return tuple(torch.stack([x[i] for x in ws]) for i in range(4))
+        try:
+            parity = sampled_parity(out, ti, ridx, rw, bank_fn, offset)
+        except Exception as exc:  # noqa: BLE001 -- reported in the line
+            parity = {"ok": False, "error": f"{type(exc).__name__}: {exc}"}
+        if world > 1:
+            parity["note"] = (f"rank 0's tokens after the exchange over {world} ranks, against all the experts "
+                              f"they reach (weights regenerated on rank 0 by global expert id)")
+    barrier()
 
     # roofline of the dominant kernel (GEMM1: 2/3 of the layer's FLOPs)
     g1_ms, g1_n = prof["gemm1_swiglu"]
-    g2_ms, g2_n = prof["gemm2_weighted"]
     total_launches = sum(n for _, n in prof.values())   # launches in K profiled steps = launches in K timed steps
     roofline = None
     if g1_n and pairs is not None and args.workload == "decode":
@@ -527,24 +743,27 @@ def main():
     elif g1_n and pairs is not None:
         g1_avg = g1_ms / g1_n
         achieved = GEMM1_FLOP_PER_PAIR * pairs / (g1_avg / 1e3) / 1e12
-        peak = 2.0 * peaks["bf16_sustained"]
-        # DRAM bytes of one GEMM1 launch from an ncu capture of this exact workload (N = 1, 256 local
-        # experts, T = 8192): profiles/launches_ep_layer_T8192.md.  Other workloads: not captured.
-        traffic = 12.01e9 if (args.workload == "ep" and world == 1 and T == 8192) else None
-        roofline = {"bound": "tensor", "kernel": "gemm1_swiglu", "achieved": achieved, "peak": peak,
-                    "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
-                    "traffic_note": "DRAM bytes per launch (ncu dram__bytes_read+write); algorithmic 8.26e9"
-                                    if traffic else None,
-                    "peak_note": f"FP8 dense = 2 x {peaks['source']} sustained cuBLAS bf16 "
-                                 f"({peaks['bf16_sustained']} TFLOP/s)",
-                    "avg_launch_ms": g1_avg}
+        fp8 = fp8_peak(peaks)
+        traffic, tnote = gemm1_traffic(name) if world == 1 else (None, "captured at N = 1 only")
+        roofline = {"bound": "tensor", "kernel": "gemm1_swiglu", "achieved": achieved, "peak": fp8["peak"],
+                    "unit": "TFLOP/s", "frac": achieved / fp8["peak"], "traffic": traffic, "traffic_note": tnote,
+                    "algorithmic_bytes": (active or 0) * (W13_BYTES_PER_EXPERT + W13_SCALE_BYTES)
+                                         + pairs * (H + (H // 128) * 4 + 2 * I + (I // 128) * 4),
+                    "peak_note": fp8["peak_note"], "avg_launch_ms": g1_avg,
+                    "frac_of_2x_sustained_bf16": achieved / (2.0 * peaks["bf16_sustained"])}
     kernels = {k: {"ms_per_launch": (v[0] / v[1]) if v[1] else None, "launches": v[1],
                    "share": (v[0] / sum(x[0] for x in prof.values())) if v[1] else 0.0}
                for k, v in prof.items()}
 
+    extra = None
+    if rank == 0 and world == 1 and not args.no_extra:
+        try:
+            extra = single_gpu_configs(B, S, dev, peaks, wb if E == E_GLOBAL else None)
+        except Exception as exc:  # noqa: BLE001 -- reported in the line
+            extra = {"error": f"{type(exc).__name__}: {exc}"}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = measure_cpu_baseline(T, E, offset)
+        cpu = measure_cpu_baseline(T, E, offset, routing_bias=zipf_cpu_bias() if args.zipf else None)
     try:
         clock_summary = clocks.summary([(t_wall0, t_wall1, "timed steps"),
                                         (t_wall0, t_wall2, "timed steps + the same steps profiled")])
@@ -556,18 +775,15 @@ def main():
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "fp8_e4m3 (fp32 accumulate)", "data": "synthetic",
-            "config": {"workload": name, "tokens_per_gpu": T, "local_experts_per_gpu": E,
-                       "global_experts": E_GLOBAL, "hidden": H, "intermediate": I, "top_k": 8,
-                       "parallelism": f"ep{world}", "ep_exchange": args.ep_exchange if world > 1 else None,
-                       "l2": "inputs larger than L2 (weights stream from HBM)",
-                       "pairs_rank0": pairs, "cuda_graph": bool(args.graph and world == 1)},
+            "config": line_config(name, T, E, world, args),
+            "pairs_rank0": pairs,
             "p50_step_ms": step_ms[len(step_ms) // 2], "p90_step_ms": step_ms[int(len(step_ms) * 0.9)],
             "tflops_per_gpu": (FLOP_PER_PAIR * pairs / (ms_per_step / 1e3) / 1e12) if pairs else None,
-            "layer_hbm_gbs": (active * (W13_BYTES_PER_EXPERT + W2_BYTES_PER_EXPERT + W13_SCALE_BYTES + W2_SCALE_BYTES)
-                              / (ms_per_step / 1e3) / 1e9) if active else None,
+            "layer_hbm_gbs": (active * EXPERT_BYTES / (ms_per_step / 1e3) / 1e9) if active else None,
             "active_local_experts": active,
             "roofline": roofline, "kernels": kernels, "gpu_launches": total_launches,
-            "e2e": e2e, "cpu_baseline": cpu,
+            "e2e": e2e, "cpu_baseline": cpu, "parity": parity,
+            "single_gpu_configs": extra,
             "clocks": clock_summary,
         }
         print(json.dumps(line), flush=True)
