@@ -382,13 +382,15 @@ def run_reference(args, world, rank):
 
 
 # ------------------------------------------------------------------- parity --
-def sampled_parity(out, ti, idx, w, bank_fn, offset_of, n_sample: int = 256, seed: int = 5) -> dict:
+def sampled_parity(out, ti, idx, w, bank_fn, expert_range, n_sample: int = 256, seed: int = 5) -> dict:
     """The step's output on a seeded sample of tokens against the fp32 reference (the oracle's
     expert math on this GPU, ``oracle/moe_oracle.py``), with the layer's acceptance test.
 
     ``idx``/``w``: the step's routing of these tokens (int32 ids, weights [T, 8]), checked for
-    every token against the oracle's routing on the CPU; ``bank_fn(global_ids)`` returns the
-    weights of those experts stacked in the given (ascending) order."""
+    every token against the oracle's routing on the CPU.  ``expert_range`` = (lo, hi): the global
+    experts the output covers (the local experts at N = 1, all 256 after the expert-parallel
+    exchange); other ids contribute nothing, as in the layer.  ``bank_fn(global_ids)`` returns
+    the weights of those experts stacked in the given (ascending) order."""
     from oracle import moe_oracle as O
     T = int(out.shape[0])
     ref_idx, _ = O.route(ti.routing_logits.float().cpu(), ti.routing_bias.cpu(), 2.5)
@@ -396,12 +398,16 @@ def sampled_parity(out, ti, idx, w, bank_fn, offset_of, n_sample: int = 256, see
     g = torch.Generator().manual_seed(seed)
     sel = torch.randperm(T, generator=g)[:min(T, n_sample)].sort().values.to(out.device)
     sidx = idx[sel].long()
-    experts = sorted(set(sidx.flatten().tolist()))
-    wb = bank_fn(experts)
-    remap = torch.full((E_GLOBAL,), -1, dtype=torch.long, device=out.device)
-    remap[torch.tensor(experts, device=out.device)] = torch.arange(len(experts), device=out.device)
-    ref = O.moe_experts(remap[sidx].to(torch.int32), w[sel], ti.hidden_states[sel], ti.hidden_states_scale[:, sel],
-                        *wb, 0).to(torch.bfloat16)
+    lo, hi = expert_range
+    experts = sorted(e for e in set(sidx.flatten().tolist()) if lo <= e < hi)
+    if experts:
+        wb = bank_fn(experts)
+        remap = torch.full((E_GLOBAL,), -1, dtype=torch.long, device=out.device)
+        remap[torch.tensor(experts, device=out.device)] = torch.arange(len(experts), device=out.device)
+        ref = O.moe_experts(remap[sidx].to(torch.int32), w[sel], ti.hidden_states[sel],
+                            ti.hidden_states_scale[:, sel], *wb, 0).to(torch.bfloat16)
+    else:   # no sampled token reaches an expert the output covers: zero rows
+        ref = torch.zeros((sel.numel(), H), dtype=torch.bfloat16, device=out.device)
     res = O.check_tolerance(out[sel], ref)
     return {"ok": bool(res["ok"] and routing_exact), "routing_exact_all_tokens": routing_exact,
             "tokens_checked": int(sel.numel()), "experts_checked": len(experts),
@@ -580,6 +586,26 @@ def main():
         if world > 1:
             torch.distributed.barrier()
 
+    # At N > 1, rank 0 first times its own shard on one GPU at the same pair load an expert-parallel
+    # rank carries (N x T tokens routed over all experts give each shard of 256/N experts about
+    # 8 x T pairs): the baseline of the scaling efficiency at equal per-GPU work.
+    equal_load = None
+    if world > 1 and args.workload == "ep":
+        if rank == 0:
+            t_ref = world * T
+            tr_in = S.token_inputs(t_ref, seed=99, device=dev)
+            ref_call = lambda: B.kernel(tr_in.routing_logits, tr_in.routing_bias, tr_in.hidden_states,
+                                        tr_in.hidden_states_scale, wb.gemm1_weights, wb.gemm1_weights_scale,
+                                        wb.gemm2_weights, wb.gemm2_weights_scale, offset, 2.5)
+            ms_ref = time_calls(ref_call, 5, 3)
+            ridx, _ = B.route(tr_in.routing_logits, tr_in.routing_bias, 2.5)
+            ref_pairs = int(((ridx >= offset) & (ridx < offset + E)).sum().item())
+            equal_load = {"tokens": t_ref, "local_experts": E, "pairs": ref_pairs, "p50_ms": ms_ref[len(ms_ref) // 2]}
+            del tr_in
+            B.release_workspaces()
+            torch.cuda.empty_cache()
+        barrier()
+
     for _ in range(args.warmup):
         step(ti.routing_logits, ti.routing_bias, ti.hidden_states, ti.hidden_states_scale)
     torch.cuda.synchronize(dev)
@@ -719,7 +745,7 @@ def main():
                 ws = [S.expert_weights(g, seed=0, device=dev) for g in experts]
                 return tuple(torch.stack([x[i] for x in ws]) for i in range(4))
         try:
-            parity = sampled_parity(out, ti, ridx, rw, bank_fn, offset)
+            parity = sampled_parity(out, ti, ridx, rw, bank_fn, (offset, offset + E) if world == 1 else (0, E_GLOBAL))
         except Exception as exc:  # noqa: BLE001 -- reported in the line
             parity = {"ok": False, "error": f"{type(exc).__name__}: {exc}"}
         if world > 1:
@@ -770,6 +796,9 @@ def main():
     except Exception as exc:  # noqa: BLE001
         clock_summary = {"sm_mhz": None, "reasons": ["unsampled"], "error": f"{type(exc).__name__}: {exc}"}
 
+    if equal_load is not None:
+        equal_load["efficiency_vs_ep_step"] = equal_load["p50_ms"] / ms_per_step
+        equal_load["ep_pairs_rank0"] = pairs
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -782,7 +811,7 @@ def main():
             "layer_hbm_gbs": (active * EXPERT_BYTES / (ms_per_step / 1e3) / 1e9) if active else None,
             "active_local_experts": active,
             "roofline": roofline, "kernels": kernels, "gpu_launches": total_launches,
-            "e2e": e2e, "cpu_baseline": cpu, "parity": parity,
+            "e2e": e2e, "cpu_baseline": cpu, "parity": parity, "equal_load_1gpu": equal_load,
             "single_gpu_configs": extra,
             "clocks": clock_summary,
         }

@@ -30,7 +30,7 @@ TOP_K = 8
 
 _LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libkf_moe.so")
 _lib = None
-_lib_lock = threading.Lock()
+_lib_lock = threading.RLock()   # extension() loads the library while holding it
 
 KF_OK = 0
 KF_ERR_DEVICE_STATUS = 6

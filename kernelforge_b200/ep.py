@@ -20,8 +20,9 @@ By default the rows and the partials move by stores into the ranks' symmetric
 buffers (``PeerExchange``): the pack kernel writes each row straight into its
 destination's receive area and the expert stage's reduce kernel writes each
 partial back into its source's return area, with the library's bounded barrier
-between the phases; reading the count matrix is the one host synchronisation
-of a step.
+between the phases.  The host reads the count matrix (it sizes the expert
+call) from an asynchronous copy, waiting only for the plan, not for the pack
+that the GPU runs meanwhile.
 With ``exchange="nccl"`` the same kernels run around ``torch.distributed``
 all-to-alls over NCCL (split sizes first, then rows).
 """
@@ -82,6 +83,7 @@ class PeerExchange:
         self.status = self.meta[world * world:]
         self.recv = self.buf[self.off_recv:self.off_recv + self.recv_cap * ROW_BYTES].view(self.recv_cap, ROW_BYTES)
         self.back = self.buf[self.off_back:self.off_back + self.send_cap * H * 2].view(torch.bfloat16).view(-1, H)
+        self.meta_host = torch.empty(world * world + 1, dtype=torch.int32).pin_memory()   # count matrix + status
         self.epoch = 0
 
     def barrier(self, stream) -> None:
@@ -155,6 +157,8 @@ class ExpertParallelMoE:
     def local_pairs(self) -> int:
         """(row, local expert) pairs this rank's expert kernels processed in the last forward (synchronises)."""
         ids = getattr(self, "_last_ids", None)
+        if callable(ids):
+            ids = ids()
         if ids is None:
             return 0
         loc = ids.to(torch.int64) - self.offset
@@ -231,37 +235,50 @@ class ExpertParallelMoE:
         hs = hidden_states_scale.contiguous() if hidden_states_scale is not None else None
         if hs is None and hid.dtype != torch.bfloat16:
             raise ValueError("without hidden_states_scale, hidden_states must be bf16 rows")
-        stream = torch.cuda.current_stream(dev).cuda_stream
+        cstream = torch.cuda.current_stream(dev)
+        stream = cstream.cuda_stream
         ws = B._ep_workspace(dev, int(lib.kf_ep_workspace_bytes(T, world)))
         sz = ctypes.c_size_t(ws.numel())
+        pos = torch.empty((T, world), dtype=torch.int32, device=dev)
 
-        def plan(pe):
+        def plan_and_pack(pe):
+            """Enqueue plan, barrier, an asynchronous copy of the count matrix, pack and barrier;
+            returns the event that marks the copy."""
             B._check(lib.kf_ep_plan_p2p(B._ptr(idx), T, world, rank, pe.peer_counts.data_ptr(), B._ptr(ws), sz,
                                         stream), "kf_ep_plan_p2p")
             pe.barrier(stream)                  # every rank's count row has landed here
-            meta = pe.meta.cpu()                # the step's one host synchronisation
-            err = peer_status_error(int(meta[world * world]))
+            pe.meta_host.copy_(pe.meta, non_blocking=True)
+            copied = torch.cuda.Event()
+            copied.record(cstream)
+            # the pack reads the counts on the device; rows beyond a receive area are dropped
+            # (and flagged), which the host sees below and redoes with larger areas
+            B._check(lib.kf_ep_pack_p2p(B._ptr(idx), B._ptr(w), B._ptr(hid), B._ptr(hs), T, world, rank,
+                                        pe.counts.data_ptr(), pe.peer_recv.data_ptr(), pe.recv_cap, B._ptr(pos),
+                                        pe.status.data_ptr(), B._ptr(ws), sz, stream), "kf_ep_pack_p2p")
+            pe.barrier(stream)                  # every row sent to this rank has landed
+            return copied
+
+        def read_counts(pe, copied):
+            copied.synchronize()                # the plan only; the GPU packs meanwhile
+            err = peer_status_error(int(pe.meta_host[world * world]))
             if err:
                 raise RuntimeError(err)
-            return meta[:world * world].view(world, world)
+            return pe.meta_host[:world * world].clone().view(world, world)
 
-        counts = plan(self._peer)
+        pe = self._peer
+        counts = read_counts(pe, plan_and_pack(pe))
         # every rank holds the same count matrix, so all of them take this branch together
         need_recv, need_send = peer_capacity_needs(counts)
-        if need_recv > self._peer.recv_cap or need_send > self._peer.send_cap:
-            self._peer = PeerExchange(max(need_recv, self._peer.recv_cap), max(need_send, self._peer.send_cap),
-                                      world, rank, self.group, dev)
-            counts = plan(self._peer)
-        pe = self._peer
+        if need_recv > pe.recv_cap or need_send > pe.send_cap:
+            cstream.synchronize()               # the dropped pack has finished with the old areas
+            self._peer = PeerExchange(max(need_recv, pe.recv_cap), max(need_send, pe.send_cap), world, rank,
+                                      self.group, dev)
+            pe = self._peer
+            counts = read_counts(pe, plan_and_pack(pe))
         R = int(counts[:, rank].sum())
         S = int(counts[rank, :].sum())
-        pos = torch.empty((T, world), dtype=torch.int32, device=dev)
-        B._check(lib.kf_ep_pack_p2p(B._ptr(idx), B._ptr(w), B._ptr(hid), B._ptr(hs), T, world, rank,
-                                    pe.counts.data_ptr(), pe.peer_recv.data_ptr(), pe.recv_cap, B._ptr(pos),
-                                    pe.status.data_ptr(), B._ptr(ws), sz, stream), "kf_ep_pack_p2p")
-        pe.barrier(stream)                      # every row sent to this rank has landed
         recv = pe.recv[:R]
-        self._last_ids = recv[:, H + HB * 4:H + HB * 4 + TOP_K * 4].contiguous().view(torch.int32)
+        self._last_ids = lambda: recv[:, H + HB * 4:H + HB * 4 + TOP_K * 4].contiguous().view(torch.int32)
         # the experts' last kernel (the reduce) stores each row's partial straight into
         # its source's return buffer
         B.experts_packed_p2p(recv, self.w.gemm1_weights, self.w.gemm1_weights_scale, self.w.gemm2_weights,

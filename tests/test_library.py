@@ -170,3 +170,14 @@ def test_torch_extension_binds_the_c_abi():
         ext.kernel(ti.routing_logits, ti.routing_bias, ti.hidden_states, ti.hidden_states_scale, wb.gemm1_weights,
                    wb.gemm1_weights_scale, wb.gemm2_weights, wb.gemm2_weights_scale, 0, 2.5)
     ext.release_workspaces()
+
+
+def test_extension_loads_first_in_a_fresh_process():
+    """A process whose first call into the binding is the extension (as kernel() is for a caller that
+    never routes first) loads the library and the extension without deadlocking."""
+    import subprocess
+    import sys
+    code = ("import sys; sys.path.insert(0, %r); from kernelforge_b200 import binding as B; "
+            "ext = B.extension(); print(callable(ext.kernel))" % ROOT)
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and r.stdout.strip().endswith("True"), r.stderr[-2000:]
