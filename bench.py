@@ -520,7 +520,12 @@ def single_gpu_configs(B, S, dev, peaks, bank256) -> dict:
 
 # DRAM bytes per GEMM1 launch from ncu captures (dram__bytes_read.sum + dram__bytes_write.sum), valid
 # only for the kernel source they were captured on: the line reports null once the source changes.
-TRAFFIC = {}
+TRAFFIC = {
+    "ep_layer_T8192_per_gpu_256_experts": {
+        "bytes": 8 * (1_235_064_576 + 33_124_608), "source_sha16": "ab4f12be5b3b2fa8",
+        "note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of gemm1_swiglu_kernel on a 1/8 replica "
+                "(8192 tokens, 32 local experts: the same pairs per expert), scaled by 8 experts' worth"},
+}
 
 
 def gemm1_traffic(name: str):
