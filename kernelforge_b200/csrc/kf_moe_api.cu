@@ -257,7 +257,7 @@ int run_experts(const Workspace& w, void* ws, const RowLayout& in, const void* w
 
   {
     ProfScope ps(KF_KERNEL_REDUCE, s);
-    if (launch_reduce(ws_ptr<int32_t>(ws, w.token_slot), ws_ptr<float>(ws, w.y), T, out, out_fp32, po, 4 * num_sms,
+    if (launch_reduce(ws_ptr<int32_t>(ws, w.token_slot), ws_ptr<float>(ws, w.y), T, out, out_fp32, po, 2 * num_sms,
                       s) !=
         cudaSuccess)
       return KF_ERR_CUDA;

@@ -266,6 +266,35 @@ __global__ void __launch_bounds__(kMaxLocalExperts) permute_scan_kernel(
   }
 }
 
+// A token's row of token_slot lists its permuted rows in ascending order (the
+// local experts ascending: segments lie in expert order), then -1 for the other
+// pairs, so the reduce reads them in the reference's index_add_ order with no
+// sort.  A local expert repeated among a token's ids (outside the routing
+// contract) counts once, at its first position, so every listed row is distinct.
+__device__ __forceinline__ bool pair_is_local_first(const int32_t* ids, int k, int offset, int E) {
+  const int e = ids[k], le = e - offset;
+  if (e < 0 || le < 0 || le >= E) return false;
+#pragma unroll
+  for (int j = 0; j < kTopK; ++j)
+    if (j < k && ids[j] == e) return false;
+  return true;
+}
+
+// Position of pair k in its token's token_slot row (ids = the token's 8 ids).
+__device__ __forceinline__ int token_slot_position(const int32_t* ids, int k, int offset, int E) {
+  uint32_t local = 0;  // bit j: pair j is listed as a row
+#pragma unroll
+  for (int j = 0; j < kTopK; ++j) local |= pair_is_local_first(ids, j, offset, E) ? (1u << j) : 0u;
+  if ((local >> k) & 1u) {
+    const int e = ids[k];
+    int pos = 0;
+#pragma unroll
+    for (int j = 0; j < kTopK; ++j) pos += (((local >> j) & 1u) && ids[j] < e) ? 1 : 0;
+    return pos;
+  }
+  return __popc(local) + __popc(~local & ((1u << k) - 1u));
+}
+
 // Per chunk: each local pair gets its permuted row (slot) = expert segment start +
 // pairs of that expert in earlier chunks + earlier tokens of this chunk with the
 // same expert (popcount of the mask below the token).  Stable and deterministic:
@@ -279,10 +308,15 @@ __global__ void __launch_bounds__(256) permute_assign_kernel(
   grid_dep_wait();
   __shared__ uint4 masks[kMaxLocalExperts];
   __shared__ int32_t base[kMaxLocalExperts];
+  __shared__ int32_t ids[kChunkTokens * kTopK];
   const int chunk = blockIdx.x;
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     masks[e] = chunk_masks[static_cast<size_t>(chunk) * E + e];
     base[e] = meta->expert_pad_start[e] + chunk_base[static_cast<size_t>(chunk) * E + e];
+  }
+  for (int p = threadIdx.x; p < kChunkTokens * kTopK; p += blockDim.x) {
+    const int t = chunk * kChunkTokens + (p >> 3);
+    ids[p] = t < T ? in.idx(t, p & 7) : -1;
   }
   __syncthreads();
   for (int p = threadIdx.x; p < kChunkTokens * kTopK; p += blockDim.x) {
@@ -290,10 +324,9 @@ __global__ void __launch_bounds__(256) permute_assign_kernel(
     const int t = chunk * kChunkTokens + tl;
     if (t >= T) break;
     const size_t ti = static_cast<size_t>(t) * kTopK + (p & 7);
-    const int e = in.idx(t, p & 7);
-    const int le = e - offset;
+    const int le = ids[p] - offset;
     int slot = -1;
-    if (e >= 0 && le >= 0 && le < E) {
+    if (pair_is_local_first(ids + tl * kTopK, p & 7, offset, E)) {
       const uint4 m = masks[le];
       const int w = tl >> 5;
       const uint32_t below = (1u << (tl & 31)) - 1u;
@@ -311,7 +344,7 @@ __global__ void __launch_bounds__(256) permute_assign_kernel(
         slot_pair[slot] = static_cast<int32_t>(ti);
       }
     }
-    token_slot[ti] = slot;
+    token_slot[static_cast<size_t>(t) * kTopK + token_slot_position(ids + tl * kTopK, p & 7, offset, E)] = slot;
   }
 }
 
@@ -437,9 +470,9 @@ __global__ void __launch_bounds__(kFrontThreads) front_small_kernel(
   if (tid == 0) meta->num_pairs = total_pairs;
   // stable slots: segment start + earlier tokens of the same expert
   for (int p = tid; p < T * kTopK; p += kFrontThreads) {
-    const int e = tk[p], le = e - offset, t = p >> 3;
+    const int le = tk[p] - offset, t = p >> 3;
     int slot = -1;
-    if (e >= 0 && le >= 0 && le < E) {
+    if (pair_is_local_first(tk + t * kTopK, p & 7, offset, E)) {
       const int w = t >> 5;
       int r = __popc(masks[le * 4 + w] & ((1u << (t & 31)) - 1u));
       for (int q = 0; q < w; ++q) r += __popc(masks[le * 4 + q]);
@@ -454,7 +487,7 @@ __global__ void __launch_bounds__(kFrontThreads) front_small_kernel(
         pairs[atomicAdd(&npairs, 1)] = make_int2(t, slot);
       }
     }
-    token_slot[p] = slot;
+    token_slot[t * kTopK + token_slot_position(tk + t * kTopK, p & 7, offset, E)] = slot;
   }
   __syncthreads();
   // gather: one warp per local pair
@@ -474,12 +507,29 @@ __global__ void __launch_bounds__(kFrontThreads) front_small_kernel(
 
 // out[t] = sum of the token's permuted rows of y (already routing-weighted), in
 // ascending row order (= ascending local expert, the reference's index_add_ order),
-// accumulated in fp32 and rounded once.  CTAs stride over the rows; a thread owns
-// 8 consecutive columns (two 16-byte loads per row of y, one 16-byte store).
-constexpr int kReduceThreads = 224;   // 7 warps: a row's 896 column groups in 4 passes
+// accumulated in fp32 from zero and rounded once.  Each CTA walks its tokens
+// t = blockIdx.x + i * gridDim.x in batches of whole tokens with at most
+// kReduceBatch rows between them: warp 0 lists a batch's rows and output rows in
+// shared memory, then each thread loads its 4 columns of every row of the batch
+// at once and sums them token by token.  So a call whose tokens have one local
+// row each (a GPU holding 32 of the 256 experts) keeps as many loads in flight as
+// one whose tokens have eight.
+constexpr int kReduceThreads = 448;   // 14 warps: a row's 1792 float4 columns in 4 passes
+constexpr int kReduceBatch = 8;       // rows of y per batch (a token has at most 8)
 constexpr int kMaxWorld = 64;
 
-__global__ void __launch_bounds__(kReduceThreads) unpermute_reduce_kernel(const int32_t* __restrict__ token_slot,
+__device__ __forceinline__ void reduce_store(char* row, bool f32, int c, const float4& v) {
+  if (!row) return;
+  if (f32) {
+    reinterpret_cast<float4*>(row)[c] = v;
+  } else {
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+    reinterpret_cast<uint2*>(row)[c] =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+  }
+}
+
+__global__ void __launch_bounds__(kReduceThreads, 2) unpermute_reduce_kernel(const int32_t* __restrict__ token_slot,
                                                      const float* __restrict__ y, int T, void* __restrict__ out,
                                                      int out_fp32, const PeerOut po) {
   grid_dep_wait();
@@ -489,6 +539,10 @@ __global__ void __launch_bounds__(kReduceThreads) unpermute_reduce_kernel(const 
   // rows of sources <= s, src_base[s] = (return row) - (received row) for source s.
   __shared__ int32_t src_end[kMaxWorld];
   __shared__ int32_t src_base[kMaxWorld];
+  __shared__ int32_t b_slot[kReduceBatch];  // the batch's rows of y, token after token
+  __shared__ int32_t b_end[kReduceBatch];   // token j's rows are b_slot[b_end[j-1] .. b_end[j])
+  __shared__ char* b_dst[kReduceBatch];     // token j's output row (null: not stored)
+  __shared__ int32_t b_tokens;
   if (po.peer_back) {
     const int s = threadIdx.x;
     int n = 0, so = 0;
@@ -509,63 +563,81 @@ __global__ void __launch_bounds__(kReduceThreads) unpermute_reduce_kernel(const 
     }
     __syncthreads();
   }
-  for (int t = blockIdx.x; t < T; t += gridDim.x) {
-    uint4* dst16 = nullptr;
-    if (po.peer_back) {
-      // a row past the received total (T larger than the count matrix says) has no
-      // place in any source's send order and is not stored; uniform over the block
-      int s = 0;
-      while (s < po.world && t >= src_end[s]) ++s;
-      if (s == po.world) continue;
-      dst16 = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(po.peer_back[s]) +
-                                       static_cast<size_t>(src_base[s] + t) * kH);
-    } else if (!out_fp32) {
-      dst16 = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + static_cast<size_t>(t) * kH);
-    }
-    int sl[8];
-    int n = 0;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int v = token_slot[static_cast<size_t>(t) * kTopK + k];
-      sl[k] = v < 0 ? 0x7fffffff : v;
-      n += v >= 0 ? 1 : 0;
-    }
-    // sort ascending (8-element odd-even transposition network)
-#pragma unroll
-    for (int r = 0; r < 8; ++r) {
-#pragma unroll
-      for (int k = (r & 1); k + 1 < 8; k += 2) {
-        const int a = sl[k], b = sl[k + 1];
-        sl[k] = min(a, b);
-        sl[k + 1] = max(a, b);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool f32 = out_fp32 && !po.peer_back;
+  const int ntok = static_cast<int>(blockIdx.x) < T ? (T - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1 : 0;
+  for (int i0 = 0; i0 < ntok;) {
+    if (warp == 0) {
+      // lane l looks at this CTA's token i0 + l; the batch is the longest run of
+      // them (at most kReduceBatch tokens) whose rows number at most kReduceBatch
+      // -- never empty, as a token has at most 8 rows
+      const int i = i0 + lane;
+      const int t = static_cast<int>(blockIdx.x) + i * static_cast<int>(gridDim.x);
+      int4 a = make_int4(-1, -1, -1, -1), b = a;
+      if (i < ntok) {
+        const int4* ts = reinterpret_cast<const int4*>(token_slot + static_cast<size_t>(t) * kTopK);
+        a = ts[0];
+        b = ts[1];
       }
-    }
-    for (int g = threadIdx.x; g < kH / 8; g += blockDim.x) {
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      const int sl[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      int n = 0;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        if (k < n) {
-          const float4* src = reinterpret_cast<const float4*>(y + static_cast<size_t>(sl[k]) * kH) + 2 * g;
-          const float4 a = src[0], b = src[1];
-          acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
-          acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+      for (int k = 0; k < 8; ++k) n += sl[k] >= 0 ? 1 : 0;
+      int incl = n;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      const bool take = i < ntok && lane < kReduceBatch && incl <= kReduceBatch;
+      const unsigned tm = __ballot_sync(0xffffffffu, take);
+      if (take) {
+        int pos = incl - n;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (sl[k] >= 0) b_slot[pos++] = sl[k];  // listed rows are ascending; -1 only past them
+        b_end[lane] = incl;
+        char* d = nullptr;
+        if (po.peer_back) {
+          // a row past the received total has no place in any source's send order
+          int s = 0;
+          while (s < po.world && t >= src_end[s]) ++s;
+          if (s < po.world)
+            d = static_cast<char*>(po.peer_back[s]) + static_cast<size_t>(src_base[s] + t) * kH * 2;
+        } else {
+          d = static_cast<char*>(out) + static_cast<size_t>(t) * kH * (f32 ? 4 : 2);
+        }
+        b_dst[lane] = d;
+      }
+      if (lane == 0) b_tokens = __popc(tm);
+    }
+    __syncthreads();
+    const int nt = b_tokens;
+    const int ne = b_end[nt - 1];
+    for (int c = threadIdx.x; c < kH / 4; c += kReduceThreads) {
+      float4 v[kReduceBatch];
+#pragma unroll
+      for (int e = 0; e < kReduceBatch; ++e)
+        if (e < ne) v[e] = __ldg(reinterpret_cast<const float4*>(y + static_cast<size_t>(b_slot[e]) * kH) + c);
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      int j = 0;
+      while (j < nt && b_end[j] == 0) reduce_store(b_dst[j++], f32, c, acc);  // tokens without a local row
+#pragma unroll
+      for (int e = 0; e < kReduceBatch; ++e) {
+        if (e < ne) {
+          acc.x += v[e].x;
+          acc.y += v[e].y;
+          acc.z += v[e].z;
+          acc.w += v[e].w;
+          while (j < nt && b_end[j] == e + 1) {
+            reduce_store(b_dst[j++], f32, c, acc);
+            acc = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
         }
       }
-      if (dst16) {
-        uint4 packed;
-        __nv_bfloat162 h0 = __floats2bfloat162_rn(acc[0], acc[1]), h1 = __floats2bfloat162_rn(acc[2], acc[3]);
-        __nv_bfloat162 h2 = __floats2bfloat162_rn(acc[4], acc[5]), h3 = __floats2bfloat162_rn(acc[6], acc[7]);
-        packed.x = *reinterpret_cast<uint32_t*>(&h0);
-        packed.y = *reinterpret_cast<uint32_t*>(&h1);
-        packed.z = *reinterpret_cast<uint32_t*>(&h2);
-        packed.w = *reinterpret_cast<uint32_t*>(&h3);
-        dst16[g] = packed;
-      } else {
-        float4* d = reinterpret_cast<float4*>(static_cast<float*>(out) + static_cast<size_t>(t) * kH) + 2 * g;
-        d[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        d[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
-      }
     }
+    i0 += nt;
+    __syncthreads();  // the batch lists are rewritten next
   }
   if (po.peer_back) __threadfence_system();
 }
