@@ -389,10 +389,13 @@ int kf_moe_forward(const float* routing_logits, const void* routing_bias, const 
   rc = ensure_device(&sms);
   if (rc != KF_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (cudaMemsetAsync(ws_ptr<int>(workspace, w.status), 0, sizeof(int), s) != cudaSuccess) return KF_ERR_CUDA;
+  const bool small = T <= kSmallT;
+  // the single-block front end clears the status word itself (one node fewer in
+  // the decode chain); the multi-block path clears it first
+  if (!small && cudaMemsetAsync(ws_ptr<int>(workspace, w.status), 0, sizeof(int), s) != cudaSuccess)
+    return KF_ERR_CUDA;
   int32_t* topk_idx = ws_ptr<int32_t>(workspace, w.topk_idx);
   float* topk_w = ws_ptr<float>(workspace, w.topk_w);
-  const bool small = T <= kSmallT;
   const RowLayout in = reference_layout(topk_idx, topk_w, hidden_states, hidden_states_scale, T);
   if (small) {
     rc = run_front_small(w, workspace, routing_logits, routing_bias, routed_scaling_factor, in, T, E,
@@ -435,8 +438,8 @@ int experts_common(const RowLayout& in, const void* gemm1_weights, const float* 
   if (rc != KF_OK) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int* status = ws_ptr<int>(workspace, w.status);
-  if (cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess) return KF_ERR_CUDA;
   const bool small = T <= kSmallT;
+  if (!small && cudaMemsetAsync(status, 0, sizeof(int), s) != cudaSuccess) return KF_ERR_CUDA;
   if (small) {
     rc = run_front_small(w, workspace, nullptr, nullptr, 0.f, in, T, E, offset, s);
     if (rc != KF_OK) return rc;

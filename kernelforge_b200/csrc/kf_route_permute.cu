@@ -68,69 +68,65 @@ __device__ __forceinline__ void route_one_token(const float* __restrict__ logits
 #pragma unroll
   for (int g = 0; g < 8; ++g) rank += better(gs[g], g, gs[my_group], my_group) ? 1 : 0;
   uint32_t avail = (rank < 4) ? 0xFFu : 0u;
-  // top-8 over the kept experts by biased score (ties: lower expert id wins)
+  // top-8 over the kept experts by biased score (ties: lower expert id wins).
+  // Scores are compared as order-preserving unsigned keys (sb is finite and
+  // never -0: it is a positive sigmoid plus a finite bias), so one warp max-
+  // reduction per round finds the best score; of the lanes holding it the
+  // lowest wins, and within a lane the lowest j: ties go to the lower expert id.
+  uint32_t key[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t u = __float_as_uint(sb[j]);
+    key[j] = ((avail >> j) & 1u) ? ((u & 0x80000000u) ? ~u : (u | 0x80000000u)) : 0u;  // 0: not a candidate
+  }
   int sel[8];
   float sel_s[8];
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
+    uint32_t bk = key[0];
+    int bj = 0;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if ((avail >> j) & 1u) {
-        if (better(sb[j], lane * 8 + j, bv, bi)) {
-          bv = sb[j];
-          bi = lane * 8 + j;
-        }
+    for (int j = 1; j < 8; ++j)
+      if (key[j] > bk) {
+        bk = key[j];
+        bj = j;
       }
-    }
+    const uint32_t wk = __reduce_max_sync(0xffffffffu, bk);
+    const int owner = __ffs(__ballot_sync(0xffffffffu, bk == wk)) - 1;
+    float mine = s[0];
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-      if (better(ov, oi, bv, bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    sel[k] = bi;
-    const int owner = bi >> 3, jj = bi & 7;
-    float mine = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-      if (j == jj) mine = s[j];
+    for (int j = 1; j < 8; ++j)
+      if (j == bj) mine = s[j];
+    sel[k] = owner * 8 + __shfl_sync(0xffffffffu, bj, owner);
     sel_s[k] = __shfl_sync(0xffffffffu, mine, owner);
-    if (lane == owner) avail &= ~(1u << jj);
+    if (lane == owner) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (j == bj) key[j] = 0u;
+    }
   }
-  // normalise the un-biased scores in ascending expert order, then scale
+  // normalise the un-biased scores, summed in ascending expert order, then
+  // scale: lane k < 8 takes selection k and its rank among the 8 ids
+  int my_e = sel[0];
+  float my_s = sel_s[0];
+#pragma unroll
+  for (int k = 1; k < 8; ++k)
+    if (lane == k) {
+      my_e = sel[k];
+      my_s = sel_s[k];
+    }
+  int my_rank = 0;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) my_rank += (sel[q] < my_e) ? 1 : 0;
   float sum = 0.f;
-  {
-    int order[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      int r = 0;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) r += (sel[q] < sel[k]) ? 1 : 0;
-      order[k] = r;
-    }
-#pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      float v = 0.f;
-#pragma unroll
-      for (int k = 0; k < 8; ++k)
-        if (order[k] == r) v = sel_s[k];
-      sum += v;
-    }
+  for (int r = 0; r < 8; ++r) {
+    const int src = __ffs(__ballot_sync(0xffffffffu, lane < 8 && my_rank == r)) - 1;
+    sum += __shfl_sync(0xffffffffu, my_s, src);
   }
   const float denom = sum + 1e-20f;
-  e_out = 0;
-  w_out = 0.f;
-#pragma unroll
-  for (int k = 0; k < 8; ++k)
-    if (k == lane) {
-      e_out = sel[k];
-      w_out = (sel_s[k] / denom) * rsf;
-    }
+  e_out = lane < 8 ? my_e : 0;
+  w_out = lane < 8 ? (my_s / denom) * rsf : 0.f;
 }
 
 __device__ __forceinline__ void load_bias8(const __nv_bfloat16* __restrict__ bias, int lane, float (&b)[8]) {
@@ -366,12 +362,15 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const Meta* __restrict
     const int t = slot_token[r];
     const uint4* src = reinterpret_cast<const uint4*>(in.row(t));
     uint4* dst = reinterpret_cast<uint4*>(a_rows + static_cast<size_t>(r) * kH);
+    // every load of the row and its scales is issued before the first store
     uint4 v[kH / 16 / 32];
 #pragma unroll
     for (int j = 0; j < kH / 16 / 32; ++j) v[j] = src[lane + 32 * j];
+    const float sc0 = in.sc(t, lane), sc1 = lane + 32 < kHB ? in.sc(t, lane + 32) : 0.f;
 #pragma unroll
     for (int j = 0; j < kH / 16 / 32; ++j) dst[lane + 32 * j] = v[j];
-    for (int kb = lane; kb < kHB; kb += 32) a_scale[static_cast<size_t>(kb) * p_cap + r] = in.sc(t, kb);
+    a_scale[static_cast<size_t>(lane) * p_cap + r] = sc0;
+    if (lane + 32 < kHB) a_scale[static_cast<size_t>(lane + 32) * p_cap + r] = sc1;
   }
 }
 
@@ -399,10 +398,15 @@ __global__ void __launch_bounds__(kFrontThreads) front_small_kernel(
   __shared__ int2 pairs[kChunkTokens * kTopK];
   __shared__ int npairs, total_pairs;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  __shared__ int bad_expert;
   for (int i = tid; i < kMaxLocalExperts * 4; i += kFrontThreads) masks[i] = 0u;
   if (tid == 0) {
     npairs = 0;
     total_pairs = 0;
+    bad_expert = 0;
+    // this kernel starts the call: it clears the call's status word (every bit is
+    // recorded after the block barrier below, or by a later kernel)
+    *status = 0;
   }
   // routing, or the caller's routing
   if (logits) {
@@ -420,12 +424,13 @@ __global__ void __launch_bounds__(kFrontThreads) front_small_kernel(
   } else {
     for (int p = tid; p < T * kTopK; p += kFrontThreads) {
       const int e = in.idx(p >> 3, p & 7);
-      if (e >= kEG) record_error(status, KF_STATUS_BAD_EXPERT);
+      if (e >= kEG) bad_expert = 1;
       tk[p] = e;
       tw[p] = in.w(p >> 3, p & 7);
     }
   }
   __syncthreads();
+  if (tid == 0 && bad_expert) record_error(status, KF_STATUS_BAD_EXPERT);
   for (int p = tid; p < T * kTopK; p += kFrontThreads) {
     const int e = tk[p], le = e - offset, t = p >> 3;
     if (e >= 0 && le >= 0 && le < E) atomicOr(&masks[le * 4 + (t >> 5)], 1u << (t & 31));
@@ -490,18 +495,30 @@ __global__ void __launch_bounds__(kFrontThreads) front_small_kernel(
     token_slot[t * kTopK + token_slot_position(tk + t * kTopK, p & 7, offset, E)] = slot;
   }
   __syncthreads();
-  // gather: one warp per local pair
+  // gather: one warp per half row of a local pair (7 x 16 bytes a lane, within
+  // the 64 registers a 1024-thread block allows), the first half also copying
+  // the row's 56 scales; every load is issued before the first store
   const int n = npairs;
-  for (int i = warp; i < n; i += kFrontThreads / 32) {
-    const int2 ts = pairs[i];
-    const uint4* src = reinterpret_cast<const uint4*>(in.row(ts.x));
-    uint4* dst = reinterpret_cast<uint4*>(a_rows + static_cast<size_t>(ts.y) * kH);
-    uint4 v[kH / 16 / 32];
+  constexpr int kHalf = kH / 16 / 32 / 2;  // 7 uint4 per lane
+  for (int i = warp; i < 2 * n; i += kFrontThreads / 32) {
+    const int2 ts = pairs[i >> 1];
+    const int h = i & 1;
+    const uint4* src = reinterpret_cast<const uint4*>(in.row(ts.x)) + h * kHalf * 32;
+    uint4* dst = reinterpret_cast<uint4*>(a_rows + static_cast<size_t>(ts.y) * kH) + h * kHalf * 32;
+    uint4 v[kHalf];
 #pragma unroll
-    for (int j = 0; j < kH / 16 / 32; ++j) v[j] = src[lane + 32 * j];
+    for (int j = 0; j < kHalf; ++j) v[j] = src[lane + 32 * j];
+    float sc0 = 0.f, sc1 = 0.f;
+    if (h == 0) {
+      sc0 = in.sc(ts.x, lane);
+      if (lane + 32 < kHB) sc1 = in.sc(ts.x, lane + 32);
+    }
 #pragma unroll
-    for (int j = 0; j < kH / 16 / 32; ++j) dst[lane + 32 * j] = v[j];
-    for (int kb = lane; kb < kHB; kb += 32) a_scale[static_cast<size_t>(kb) * p_cap + ts.y] = in.sc(ts.x, kb);
+    for (int j = 0; j < kHalf; ++j) dst[lane + 32 * j] = v[j];
+    if (h == 0) {
+      a_scale[static_cast<size_t>(lane) * p_cap + ts.y] = sc0;
+      if (lane + 32 < kHB) a_scale[static_cast<size_t>(lane + 32) * p_cap + ts.y] = sc1;
+    }
   }
 }
 
