@@ -67,8 +67,8 @@ constexpr int G2_OFF_B = 2 * G2_S * G2_A;
 constexpr int G2_OFF_BAR = G2_OFF_B + G2_S * G2_B;
 constexpr int G2_NBAR = 2 * G2_S + 4;
 constexpr int G2_OFF_MISC = G2_OFF_BAR + G2_NBAR * 8;
-// Epilogue staging for TMA stores of y: per promotion warp two halves of 32 rows x
-// 16 fp32 columns (2 KB each, 64-byte swizzled as the y tensor map expects).
+// Epilogue staging for TMA stores of y: per promotion warp 32 rows x 32 fp32
+// columns (4 KB, 128-byte swizzled as the y tensor map expects), 1024-aligned.
 constexpr int G2_STG_WARP = 32 * 32 * 4;
 constexpr int G2_OFF_STG = (G2_OFF_MISC + 16 + 1023) / 1024 * 1024;
 constexpr int G2_SMEM = G2_OFF_STG + kEpiWarps * G2_STG_WARP + 1024;
@@ -607,30 +607,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       if (live) {
         // y rows leave through TMA stores: each round the warp writes a 32-row x
-        // 16-column fp32 tile (this lane = one row) into one of its two 2 KB
-        // staging halves (64-byte swizzled, as the y tensor map expects), and one
-        // lane stores it to y.  A half is rewritten only after the store that read
-        // it two rounds earlier has read it, so the warp waits on the TMA unit only
-        // when it falls two stores behind.  Rows of the tile beyond nrows are
-        // padding rows of this tile, which nothing reads.
+        // 32-column fp32 tile (this lane = one row) into its 128-byte-swizzled
+        // staging buffer, and one lane stores it to y; the buffer is rewritten
+        // only after the previous store has read it.  Rows of the tile beyond
+        // nrows are padding rows of this tile, which nothing reads.
         const float w = row < nrows ? g.slot_weight[row0 + row] : 0.f;
         uint8_t* stg = smem + G2_OFF_STG + pw * G2_STG_WARP;
         const int xcol = nb2 * 256 + h * 128;
 #pragma unroll
-        for (int m = 0; m < 8; ++m) {
-          uint8_t* half = stg + (m & 1) * (G2_STG_WARP / 2);
-          if (lane == 0) bulk_wait_group_read1();
+        for (int m = 0; m < 4; ++m) {
+          if (lane == 0) bulk_wait_group_read0();
           __syncwarp();
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float2 p0 = acc[8 * m + 2 * j], p1 = acc[8 * m + 2 * j + 1];
-            *reinterpret_cast<float4*>(half + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
+          for (int j = 0; j < 8; ++j) {
+            const float2 p0 = acc[16 * m + 2 * j], p1 = acc[16 * m + 2 * j + 1];
+            *reinterpret_cast<float4*>(stg + lane * 128 + ((j ^ (lane & 7)) << 4)) =
                 make_float4(p0.x * w, p0.y * w, p1.x * w, p1.y * w);
           }
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tm_y, xcol + 16 * m, row0 + q * 32, half);
+            tma_store_2d(&tm_y, xcol + 32 * m, row0 + q * 32, stg);
             bulk_commit_group();
           }
         }

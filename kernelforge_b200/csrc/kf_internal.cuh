@@ -180,7 +180,7 @@ struct Gemm2Args {
 
 cudaError_t launch_gemm1(const CUtensorMap& tm_a, const CUtensorMap& tm_a32, const CUtensorMap& tm_w13,
                          const Gemm1Args& args, int grid, cudaStream_t s);
-// tm_y: fp32 [p_cap, 7168] output rows, box 16 x 32, 64-byte swizzle (TMA stores).
+// tm_y: fp32 [p_cap, 7168] output rows, box 32 x 32, 128-byte swizzle (TMA stores).
 cudaError_t launch_gemm2(const CUtensorMap& tm_chi, const CUtensorMap& tm_clo, const CUtensorMap& tm_chi32,
                          const CUtensorMap& tm_clo32, const CUtensorMap& tm_w2, const CUtensorMap& tm_y,
                          const Gemm2Args& args, int grid, cudaStream_t s);

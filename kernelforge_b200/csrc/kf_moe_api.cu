@@ -106,8 +106,7 @@ bool encode_2d_uncached(CUtensorMap* map, const void* base, int elem_bytes, uint
   const cuuint32_t elem_strides[2] = {1, 1};
   const CUresult r = g_encode(map, elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT8,
                               2, const_cast<void*>(base), dims, strides, box, elem_strides,
-                              CU_TENSOR_MAP_INTERLEAVE_NONE,
-                              box_inner * elem_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -250,7 +249,7 @@ int run_experts(const Workspace& w, void* ws, const RowLayout& in, const void* w
     ProfScope ps(KF_KERNEL_GEMM2, s);
     const int units = w.nt_cap * (kH / 256);
     CUtensorMap tm_y;
-    if (!encode_2d(&tm_y, ws_ptr<float>(ws, w.y), 4, kH, w.p_cap, 16, 32)) return KF_ERR_INVALID_ARGUMENT;
+    if (!encode_2d(&tm_y, ws_ptr<float>(ws, w.y), 4, kH, w.p_cap, 32, 32)) return KF_ERR_INVALID_ARGUMENT;
     if (launch_gemm2(tm_chi, tm_clo, tm_chi32, tm_clo32, tm_w2, tm_y, g2, units < num_sms ? units : num_sms, s) !=
         cudaSuccess)
       return KF_ERR_CUDA;
