@@ -5,8 +5,10 @@
 //   permute_scan_kernel   per-expert counts, 128-aligned segment starts and the
 //                         row-tile work list (reference: _sort_tokens :46-82 and
 //                         the tile metadata of _build_launch_tile_metadata :153-201)
-//   permute_assign_kernel stable slot of every local (token, expert) pair
+//   permute_assign_kernel stable slot of every local (token, expert) pair, and
+//                         each token's rows listed in ascending order
 //   gather_rows_kernel    gather of FP8 rows and scales into expert-contiguous rows
+//   front_small_kernel    all of the above in one block, for decode-sized calls
 //   unpermute_reduce_kernel  atomic-free unpermute-reduce into the output
 //                         (reference: the index_add_ combine :1920-1925)
 #include <cuda_bf16.h>
