@@ -522,19 +522,29 @@ def single_gpu_configs(B, S, dev, peaks, bank256) -> dict:
 # only for the kernel source they were captured on: the line reports null once the source changes.
 TRAFFIC = {
     "ep_layer_T8192_per_gpu_256_experts": {
-        "bytes": 8 * (1_235_064_576 + 33_124_608), "source_sha16": "ab4f12be5b3b2fa8",
+        "bytes": 8 * (1_220_262_656 + 33_017_344), "source_sha16": "319abe85c548e856",
         "note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of gemm1_swiglu_kernel on a 1/8 replica "
                 "(8192 tokens, 32 local experts: the same pairs per expert), scaled by 8 experts' worth"},
 }
+
+
+GEMM_SOURCES = ("kf_grouped_gemm.cu", "kf_internal.cuh", "kf_ptx.cuh", "kf_fp8.cuh")
+
+
+def gemm_source_sha16() -> str:
+    """Hash of the sources GEMM1 is compiled from (its own file and the headers it includes)."""
+    h = hashlib.sha256()
+    for name in GEMM_SOURCES:
+        with open(os.path.join(ROOT, "kernelforge_b200", "csrc", name), "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()[:16]
 
 
 def gemm1_traffic(name: str):
     rec = TRAFFIC.get(name)
     if rec is None:
         return None, "no ncu capture of this workload"
-    with open(os.path.join(ROOT, "kernelforge_b200", "csrc", "kf_grouped_gemm.cu"), "rb") as f:
-        sha = hashlib.sha256(f.read()).hexdigest()[:16]
-    if sha != rec["source_sha16"]:
+    if gemm_source_sha16() != rec["source_sha16"]:
         return None, "the GEMM kernels changed since the ncu capture"
     return rec["bytes"], rec["note"]
 

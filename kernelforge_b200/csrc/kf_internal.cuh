@@ -24,11 +24,19 @@ constexpr int kMaxLocalExperts = 256;
 // Token / row counts every entry point accepts: [0, KF_MOE_MAX_TOKENS].
 inline bool valid_tokens(int32_t n) { return n >= 0 && n <= KF_MOE_MAX_TOKENS; }
 
-// silu(x) = x * sigmoid(x) for the SwiGLU epilogues, with the hardware exp2 and
-// reciprocal approximations (a few ulp; the reference's Triton sigmoid is of the
-// same class).  Returns 0 when exp(-x) overflows, so large negative gates never
-// take a slow special-value path.
-__device__ __forceinline__ float silu_f(float x) { return x * __fdividef(1.0f, 1.0f + __expf(-x)); }
+// silu(x) = x * sigmoid(x) for the SwiGLU epilogues, from the identity
+// sigmoid(x) = (1 + tanh(x/2)) / 2: silu(x) = h + h * tanh(h) with h = x/2, one
+// hardware tanh approximation (relative error about 2^-11, below the 2^-8 of the
+// two-term FP8 intermediate it feeds) instead of an exp2 and a reciprocal.  The
+// GEMM1 epilogue runs on the special-function unit while the MMA waits, and the
+// single-op form measured 2.7 % less GEMM1 time at the config-3 layer.  Finite for
+// every finite x, with no special-value path.
+__device__ __forceinline__ float silu_f(float x) {
+  const float h = 0.5f * x;
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(h));
+  return fmaf(h, t, h);
+}
 
 // Per-call metadata written by the permute scan, read by the GEMMs and the reduce.
 struct Meta {
