@@ -570,6 +570,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const G2Unit nxt = has_next ? g2_unit(g, u + gridDim.x) : cur;
       const int nb2 = cur.nb2, row0 = cur.row0, nrows = cur.nrows;
       const bool live = q * 32 < nrows;
+      // the routing weight of this thread's row, for the epilogue: loaded as the unit
+      // starts so the L2 round trip is not on the epilogue's critical path
+      const float w = row < nrows ? g.slot_weight[row0 + row] : 0.f;
       float2 acc[64];
 #pragma unroll
       for (int j = 0; j < 64; ++j) acc[j] = make_float2(0.f, 0.f);
@@ -611,7 +614,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         // staging buffer, and one lane stores it to y; the buffer is rewritten
         // only after the previous store has read it.  Rows of the tile beyond
         // nrows are padding rows of this tile, which nothing reads.
-        const float w = row < nrows ? g.slot_weight[row0 + row] : 0.f;
         uint8_t* stg = smem + G2_OFF_STG + pw * G2_STG_WARP;
         const int xcol = nb2 * 256 + h * 128;
 #pragma unroll
