@@ -1,6 +1,6 @@
 // FP8 e4m3 helpers of the GEMM1 epilogues: the two-term (hi + lo) encoding of
-// the SwiGLU output that GEMM2 consumes.  Shared by the single-CTA and the
-// CTA-pair GEMMs, so both write bit-identical intermediates.
+// the SwiGLU output that GEMM2 consumes.  Shared by GEMM1's own epilogue and the
+// split-K finish, so both write bit-identical intermediates.
 #pragma once
 
 #include <cstdint>
