@@ -43,40 +43,65 @@ constexpr int kSmallRows = 32; // tiles with at most this many valid rows load a
 // X = A[rows, 7168] . W13[e]^T, N-block = 128 up columns + the matching 128 gate
 // columns (one MMA with N = 256).  Epilogue: silu(gate) * up, then a two-term
 // FP8 encoding (hi + lo residual) sharing one fp32 scale per 128 columns.
-constexpr int G1_S = 4;
-constexpr int G1_A = kBlk * kBlk;        // 16 KB
-constexpr int G1_B = 2 * kBlk * kBlk;    // 32 KB: up rows then gate rows
-constexpr int G1_OFF_B = G1_S * G1_A;
-constexpr int G1_OFF_AS = G1_OFF_B + G1_S * G1_B;
-constexpr int G1_OFF_WS = G1_OFF_AS + kScaleRing * kBlk * 4;
-constexpr int G1_OFF_BAR = G1_OFF_WS + kScaleRing * 8;
-constexpr int G1_NBAR = 2 * G1_S + 2 * kScaleRing + 6;
-constexpr int G1_OFF_MISC = G1_OFF_BAR + G1_NBAR * 8;
-constexpr int G1_OFF_XCH = G1_OFF_MISC + 16;
-constexpr int G1_SMEM = G1_OFF_XCH + 2 * 2 * kBlk * 4 + 1024;
+//
+// Two shared-memory layouts, as for GEMM2 below: 4 stages of 128-row A tiles, or
+// for calls with T <= 32 tokens 6 stages of 32-row A slots (4 KB; the MMA's rows
+// 32-127 then read the following shared memory and feed accumulator rows that are
+// never read), so more of W13 is in flight per SM.
+template <bool kDecode>
+struct G1Layout {
+  static constexpr int S = kDecode ? 6 : 4;
+  static constexpr int A = (kDecode ? kSmallRows : kBlk) * kBlk;  // one A slot
+  static constexpr int B = 2 * kBlk * kBlk;    // 32 KB: up rows then gate rows
+  static constexpr int OFF_B = S * A;
+  static constexpr int OFF_AS = OFF_B + S * B;
+  static constexpr int OFF_WS = OFF_AS + kScaleRing * kBlk * 4;
+  static constexpr int OFF_BAR = OFF_WS + kScaleRing * 8;
+  static constexpr int NBAR = 2 * S + 2 * kScaleRing + 6;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int OFF_XCH = OFF_MISC + 16;
+  static constexpr int SMEM = OFF_XCH + 2 * 2 * kBlk * 4 + 1024;
+  static_assert(OFF_B % 1024 == 0, "128-byte swizzled slots start on 1024-byte boundaries");
+  static_assert(SMEM <= 232448, "GEMM1 shared memory");
+  static_assert(S <= 32, "ring bitmask");
+};
 
 // ------------------------------------------------------------------ GEMM2 --
 // Y = C[rows, 2048] . W2[e]^T with C = s * (C_hi + C_lo), N-block = 256 output
 // columns.  Each K step issues two MMAs (hi and lo) into the same accumulator.
 // Epilogue: multiply by the pair's routing weight, store fp32 rows.
-constexpr int G2_S = 3;
-constexpr int G2_A = kBlk * kBlk;        // 16 KB each for hi and lo
-constexpr int G2_B = 2 * kBlk * kBlk;    // 32 KB: 256 rows of W2
-constexpr int G2_OFF_ALO = G2_S * G2_A;
-constexpr int G2_OFF_B = 2 * G2_S * G2_A;
-constexpr int G2_OFF_BAR = G2_OFF_B + G2_S * G2_B;
-constexpr int G2_NBAR = 2 * G2_S + 4;
-constexpr int G2_OFF_MISC = G2_OFF_BAR + G2_NBAR * 8;
+//
+// Two shared-memory layouts.  The general one holds 3 stages of full 128-row hi
+// and lo tiles.  The decode one serves calls with T <= 32 tokens, where no
+// expert can have more than 32 rows: it keeps only 32-row A slots (4 KB), which
+// makes room for 5 stages, so more of W2 is in flight per SM when W2 streaming
+// is the whole cost.  The MMA still spans 128 rows; in the decode layout rows
+// 32-127 of an A operand are whatever the following shared memory holds, and
+// they only feed accumulator rows that are never read.
 // Epilogue staging for TMA stores of y: per promotion warp 32 rows x 32 fp32
-// columns (4 KB, 128-byte swizzled as the y tensor map expects), 1024-aligned.
+// columns (4 KB, 128-byte swizzled as the y tensor map expects), 1024-aligned;
+// in the decode layout only the two warps of rows 0-31 store.
 constexpr int G2_STG_WARP = 32 * 32 * 4;
-constexpr int G2_OFF_STG = (G2_OFF_MISC + 16 + 1023) / 1024 * 1024;
-constexpr int G2_SMEM = G2_OFF_STG + kEpiWarps * G2_STG_WARP + 1024;
+template <bool kDecode>
+struct G2Layout {
+  static constexpr int S = kDecode ? 5 : 3;
+  static constexpr int A = (kDecode ? kSmallRows : kBlk) * kBlk;  // one hi or lo slot
+  static constexpr int B = 2 * kBlk * kBlk;                       // 32 KB: 256 rows of W2
+  static constexpr int OFF_ALO = S * A;
+  static constexpr int OFF_B = 2 * S * A;
+  static constexpr int OFF_BAR = OFF_B + S * B;
+  static constexpr int NBAR = 2 * S + 4;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int OFF_STG = (OFF_MISC + 16 + 1023) / 1024 * 1024;
+  static constexpr int STG_SLOTS = kDecode ? 2 : kEpiWarps;
+  static constexpr int SMEM = OFF_STG + STG_SLOTS * G2_STG_WARP + 1024;
+  static_assert(OFF_ALO % 1024 == 0 && OFF_B % 1024 == 0, "128-byte swizzled slots start on 1024-byte boundaries");
+  static_assert(SMEM <= 232448, "GEMM2 shared memory");
+  static_assert(S <= 32, "ring bitmask");
+};
 constexpr int kG2NB = kH / 256;  // 28 column blocks of 256
 
-static_assert(G1_SMEM <= 232448, "GEMM1 shared memory");
-static_assert(G2_SMEM <= 232448, "GEMM2 shared memory");
-static_assert(G1_S <= 32 && G2_S <= 32 && kScaleRing <= 32, "ring bitmasks");
+static_assert(kScaleRing <= 32, "ring bitmask");
 // Register split (setmaxnreg): warpgroup 0 drops to 48, warpgroups 1-2 rise to
 // 224: 128*48 + 256*224 = 63488 <= 384 threads * 168, the launch allocation
 // (__launch_bounds__(384, 1); the build checks ptxas reports 168).  ptxas
@@ -118,28 +143,30 @@ struct ArmedSlots {
   }
 };
 
+template <bool kDecode>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm1_swiglu_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_a32,
                         const __grid_constant__ CUtensorMap tm_w, const Gemm1Args g) {
   grid_dep_wait();
   grid_dep_trigger();
+  using L = G1Layout<kDecode>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sA = smem;
-  uint8_t* sB = smem + G1_OFF_B;
-  float* as_ring = reinterpret_cast<float*>(smem + G1_OFF_AS);
-  float2* ws_ring = reinterpret_cast<float2*>(smem + G1_OFF_WS);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G1_OFF_BAR);
+  uint8_t* sB = smem + L::OFF_B;
+  float* as_ring = reinterpret_cast<float*>(smem + L::OFF_AS);
+  float2* ws_ring = reinterpret_cast<float2*>(smem + L::OFF_WS);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* full = bars;
-  uint64_t* empty = full + G1_S;
-  uint64_t* sfull = empty + G1_S;
+  uint64_t* empty = full + L::S;
+  uint64_t* sfull = empty + L::S;
   uint64_t* sempty = sfull + kScaleRing;
   uint64_t* pfull = sempty + kScaleRing;
   uint64_t* pempty = pfull + 2;
   uint64_t* xbar = pempty + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + G1_OFF_MISC);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + G1_OFF_MISC + 4);
-  float* xch = reinterpret_cast<float*>(smem + G1_OFF_XCH);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+  float* xch = reinterpret_cast<float*>(smem + L::OFF_XCH);
 
   const int S = g.ksplit;
   const int kb_per = kHB / S;
@@ -148,7 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < G1_S; ++s) {
+    for (int s = 0; s < L::S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -187,8 +214,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int tile = base / kIB, nb = base % kIB;
         const int e = g.tile_expert[tile];
         const int row0 = g.tile_row0[tile];
-        const bool small = g.tile_rows[tile] <= kSmallRows;
-        const uint32_t tx = (small ? kSmallRows * kBlk : G1_A) + G1_B;
+        const bool small = kDecode || g.tile_rows[tile] <= kSmallRows;
+        const uint32_t tx = (small ? kSmallRows * kBlk : L::A) + L::B;
         const float* wsu = g.w13_scale + (static_cast<size_t>(e) * 32 + nb) * kHB;
         const float* wsg = g.w13_scale + (static_cast<size_t>(e) * 32 + kIB + nb) * kHB;
         const float su0 = wsu[lane], sg0 = wsg[lane];
@@ -209,9 +236,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         &sfull[ss.idx]);
               armed_ss.set(ss.idx, ss.ph);
               mbar_arrive_expect_tx(&full[st.idx], tx);
-              tma_load_2d(sA + st.idx * G1_A, small ? &tm_a32 : &tm_a, kb * kBlk, row0, &full[st.idx]);
-              tma_load_2d(sB + st.idx * G1_B, &tm_w, kb * kBlk, wrow_up, &full[st.idx]);
-              tma_load_2d(sB + st.idx * G1_B + G1_A, &tm_w, kb * kBlk, wrow_up + kI, &full[st.idx]);
+              tma_load_2d(sA + st.idx * L::A, small ? &tm_a32 : &tm_a, kb * kBlk, row0, &full[st.idx]);
+              tma_load_2d(sB + st.idx * L::B, &tm_w, kb * kBlk, wrow_up, &full[st.idx]);
+              tma_load_2d(sB + st.idx * L::B + L::B / 2, &tm_w, kb * kBlk, wrow_up + kI, &full[st.idx]);
               armed_st.set(st.idx, st.ph);
             }
           }
@@ -220,12 +247,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          st.advance<G1_S>();
+          st.template advance<L::S>();
           ss.advance<kScaleRing>();
         }
       }
       if (lane == 0) {  // let every copy that was issued land before the CTA can exit
-        armed_st.drain(full, G1_S, g.status);
+        armed_st.drain(full, L::S, g.status);
         armed_ss.drain(sfull, kScaleRing, g.status);
       }
     } else if (warp == 1) {
@@ -243,8 +270,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             tc_fence_after();
-            const uint32_t a0 = smem_u32(sA + st.idx * G1_A);
-            const uint32_t b0 = smem_u32(sB + st.idx * G1_B);
+            const uint32_t a0 = smem_u32(sA + st.idx * L::A);
+            const uint32_t b0 = smem_u32(sB + st.idx * L::B);
             const uint32_t d = tmem + static_cast<uint32_t>(pb.idx * 256);
 #pragma unroll
             for (int k = 0; k < kBlk / 32; ++k)
@@ -253,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_commit(&pfull[pb.idx]);
             committed = true;
             last = pb;
-            st.advance<G1_S>();
+            st.template advance<L::S>();
             pb.advance<2>();
           }
         }
@@ -425,6 +452,7 @@ __device__ __forceinline__ void g2_scales(const Gemm2Args& g, const G2Unit& w, i
   ws = __ldg(g.w2_scale + (static_cast<size_t>(w.e) * kHB + 2 * w.nb2 + h) * kIB + kb);
 }
 
+template <bool kDecode>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm2_weighted_kernel(const __grid_constant__ CUtensorMap tm_chi, const __grid_constant__ CUtensorMap tm_clo,
                           const __grid_constant__ CUtensorMap tm_chi32, const __grid_constant__ CUtensorMap tm_clo32,
@@ -432,25 +460,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                           const Gemm2Args g) {
   grid_dep_wait();
   grid_dep_trigger();
+  using L = G2Layout<kDecode>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sAhi = smem;
-  uint8_t* sAlo = smem + G2_OFF_ALO;
-  uint8_t* sB = smem + G2_OFF_B;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G2_OFF_BAR);
+  uint8_t* sAlo = smem + L::OFF_ALO;
+  uint8_t* sB = smem + L::OFF_B;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* full = bars;
-  uint64_t* empty = full + G2_S;
-  uint64_t* pfull = empty + G2_S;
+  uint64_t* empty = full + L::S;
+  uint64_t* pfull = empty + L::S;
   uint64_t* pempty = pfull + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + G2_OFF_MISC);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + G2_OFF_MISC + 4);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
 
   const int num_units = g.meta->num_tiles * kG2NB;
   if (static_cast<int>(blockIdx.x) >= num_units) return;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < G2_S; ++s) {
+    for (int s = 0; s < L::S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -485,8 +514,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int tile = u / kG2NB, nb2 = u % kG2NB;
         const int e = g.tile_expert[tile];
         const int row0 = g.tile_row0[tile];
-        const bool small = g.tile_rows[tile] <= kSmallRows;
-        const uint32_t tx = 2 * (small ? kSmallRows * kBlk : G2_A) + G2_B;
+        const bool small = kDecode || g.tile_rows[tile] <= kSmallRows;
+        const uint32_t tx = 2 * (small ? kSmallRows * kBlk : L::A) + L::B;
         const int wrow = e * kH + nb2 * 256;
         for (int kb = 0; kb < kIB; ++kb) {
           int good = 1;
@@ -494,9 +523,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             good = mbar_wait_abort(&empty[st.idx], st.ph ^ 1u, abort_flag, g.status, KF_STATUS_TIMEOUT_PRODUCER);
             if (good) {
               mbar_arrive_expect_tx(&full[st.idx], tx);
-              tma_load_2d(sAhi + st.idx * G2_A, small ? &tm_chi32 : &tm_chi, kb * kBlk, row0, &full[st.idx]);
-              tma_load_2d(sAlo + st.idx * G2_A, small ? &tm_clo32 : &tm_clo, kb * kBlk, row0, &full[st.idx]);
-              tma_load_2d(sB + st.idx * G2_B, &tm_w, kb * kBlk, wrow, &full[st.idx]);
+              tma_load_2d(sAhi + st.idx * L::A, small ? &tm_chi32 : &tm_chi, kb * kBlk, row0, &full[st.idx]);
+              tma_load_2d(sAlo + st.idx * L::A, small ? &tm_clo32 : &tm_clo, kb * kBlk, row0, &full[st.idx]);
+              tma_load_2d(sB + st.idx * L::B, &tm_w, kb * kBlk, wrow, &full[st.idx]);
               armed_st.set(st.idx, st.ph);
             }
           }
@@ -505,10 +534,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          st.advance<G2_S>();
+          st.template advance<L::S>();
         }
       }
-      if (lane == 0) armed_st.drain(full, G2_S, g.status);
+      if (lane == 0) armed_st.drain(full, L::S, g.status);
     } else if (warp == 1) {
       if (lane == 0) {
         constexpr uint32_t idesc = idesc_e4m3_f32(128, 256);
@@ -522,9 +551,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             tc_fence_after();
-            const uint32_t ahi = smem_u32(sAhi + st.idx * G2_A);
-            const uint32_t alo = smem_u32(sAlo + st.idx * G2_A);
-            const uint32_t b0 = smem_u32(sB + st.idx * G2_B);
+            const uint32_t ahi = smem_u32(sAhi + st.idx * L::A);
+            const uint32_t alo = smem_u32(sAlo + st.idx * L::A);
+            const uint32_t b0 = smem_u32(sB + st.idx * L::B);
             const uint32_t d = tmem + static_cast<uint32_t>(pb.idx * 256);
 #pragma unroll
             for (int k = 0; k < kBlk / 32; ++k) {
@@ -536,7 +565,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_commit(&pfull[pb.idx]);
             committed = true;
             last = pb;
-            st.advance<G2_S>();
+            st.template advance<L::S>();
             pb.advance<2>();
           }
         }
@@ -569,7 +598,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool has_next = u + static_cast<int>(gridDim.x) < num_units;
       const G2Unit nxt = has_next ? g2_unit(g, u + gridDim.x) : cur;
       const int nb2 = cur.nb2, row0 = cur.row0, nrows = cur.nrows;
-      const bool live = q * 32 < nrows;
+      const bool live = kDecode ? q == 0 : q * 32 < nrows;
+      // the decode layout holds 32 rows per tile; a call routed here has T <= 32
+      if (kDecode && nrows > kSmallRows && pw == 0 && lane == 0) record_error(g.status, KF_STATUS_SLOT_OVERFLOW);
       // the routing weight of this thread's row, for the epilogue: loaded as the unit
       // starts so the L2 round trip is not on the epilogue's critical path
       const float w = row < nrows ? g.slot_weight[row0 + row] : 0.f;
@@ -614,7 +645,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // staging buffer, and one lane stores it to y; the buffer is rewritten
         // only after the previous store has read it.  Rows of the tile beyond
         // nrows are padding rows of this tile, which nothing reads.
-        uint8_t* stg = smem + G2_OFF_STG + pw * G2_STG_WARP;
+        uint8_t* stg = smem + L::OFF_STG + (kDecode ? h : pw) * G2_STG_WARP;
         const int xcol = nb2 * 256 + h * 128;
 #pragma unroll
         for (int m = 0; m < 4; ++m) {
@@ -689,14 +720,26 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(const Meta* __restric
 }  // namespace
 
 cudaError_t gemm_set_attributes() {
-  cudaError_t e = cudaFuncSetAttribute(gemm1_swiglu_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, G1_SMEM);
+  cudaError_t e = cudaFuncSetAttribute(gemm1_swiglu_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       G1Layout<false>::SMEM);
   if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(gemm2_weighted_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, G2_SMEM);
+  e = cudaFuncSetAttribute(gemm1_swiglu_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           G1Layout<true>::SMEM);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(gemm2_weighted_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           G2Layout<false>::SMEM);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(gemm2_weighted_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              G2Layout<true>::SMEM);
 }
 
 cudaError_t launch_gemm1(const CUtensorMap& tm_a, const CUtensorMap& tm_a32, const CUtensorMap& tm_w13,
                          const Gemm1Args& args, int grid, cudaStream_t s) {
-  return launch_chained(gemm1_swiglu_kernel, dim3(grid), dim3(kThreads), G1_SMEM, s, tm_a, tm_a32, tm_w13, args);
+  if (args.decode)
+    return launch_chained(gemm1_swiglu_kernel<true>, dim3(grid), dim3(kThreads), G1Layout<true>::SMEM, s, tm_a, tm_a32,
+                          tm_w13, args);
+  return launch_chained(gemm1_swiglu_kernel<false>, dim3(grid), dim3(kThreads), G1Layout<false>::SMEM, s, tm_a,
+                        tm_a32, tm_w13, args);
 }
 
 cudaError_t launch_swiglu_quant(const Gemm1Args& g, int grid, cudaStream_t s) {
@@ -707,8 +750,11 @@ cudaError_t launch_swiglu_quant(const Gemm1Args& g, int grid, cudaStream_t s) {
 cudaError_t launch_gemm2(const CUtensorMap& tm_chi, const CUtensorMap& tm_clo, const CUtensorMap& tm_chi32,
                          const CUtensorMap& tm_clo32, const CUtensorMap& tm_w2, const CUtensorMap& tm_y,
                          const Gemm2Args& args, int grid, cudaStream_t s) {
-  return launch_chained(gemm2_weighted_kernel, dim3(grid), dim3(kThreads), G2_SMEM, s, tm_chi, tm_clo, tm_chi32,
-                        tm_clo32, tm_w2, tm_y, args);
+  if (args.decode)
+    return launch_chained(gemm2_weighted_kernel<true>, dim3(grid), dim3(kThreads), G2Layout<true>::SMEM, s, tm_chi,
+                          tm_clo, tm_chi32, tm_clo32, tm_w2, tm_y, args);
+  return launch_chained(gemm2_weighted_kernel<false>, dim3(grid), dim3(kThreads), G2Layout<false>::SMEM, s, tm_chi,
+                        tm_clo, tm_chi32, tm_clo32, tm_w2, tm_y, args);
 }
 
 }  // namespace kf

@@ -171,6 +171,9 @@ struct Gemm1Args {
   int32_t max_pairs;
   const int32_t* slot_pair;
   float* partial;
+  // 1 when the call has at most 32 tokens (no row tile holds more than 32 rows):
+  // GEMM1 then runs its decode layout (32-row A slots, 6 stages)
+  int32_t decode;
 };
 
 struct Gemm2Args {
@@ -184,6 +187,9 @@ struct Gemm2Args {
   float* y;                 // [p_cap][7168]
   int32_t p_cap;
   int* status;
+  // 1 when the call has at most 32 tokens, so no row tile holds more than 32
+  // rows: GEMM2 then runs its decode layout (32-row A slots, 5 stages)
+  int32_t decode;
 };
 
 cudaError_t launch_gemm1(const CUtensorMap& tm_a, const CUtensorMap& tm_a32, const CUtensorMap& tm_w13,

@@ -222,6 +222,7 @@ int run_experts(const Workspace& w, void* ws, const RowLayout& in, const void* w
   g1.max_pairs = T * kTopK;
   g1.slot_pair = ws_ptr<int32_t>(ws, w.slot_pair);
   g1.partial = ws_ptr<float>(ws, w.partial);
+  g1.decode = T <= 32 ? 1 : 0;
   {
     ProfScope ps(KF_KERNEL_GEMM1, s);
     const int units = w.nt_cap * kIB * g1.ksplit;
@@ -244,6 +245,7 @@ int run_experts(const Workspace& w, void* ws, const RowLayout& in, const void* w
   g2.y = ws_ptr<float>(ws, w.y);
   g2.p_cap = w.p_cap;
   g2.status = status;
+  g2.decode = T <= 32 ? 1 : 0;
 
   {
     ProfScope ps(KF_KERNEL_GEMM2, s);
