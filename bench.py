@@ -522,7 +522,7 @@ def single_gpu_configs(B, S, dev, peaks, bank256) -> dict:
 # only for the kernel source they were captured on: the line reports null once the source changes.
 TRAFFIC = {
     "ep_layer_T8192_per_gpu_256_experts": {
-        "bytes": 8 * (1_220_262_656 + 33_017_344), "source_sha16": "6c96ba1c74e3f015",
+        "bytes": 8 * (1_230_893_824 + 33_221_888), "source_sha16": "0034b93e9a22f1c9",
         "note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of gemm1_swiglu_kernel on a 1/8 replica "
                 "(8192 tokens, 32 local experts: the same pairs per expert), scaled by 8 experts' worth"},
 }
