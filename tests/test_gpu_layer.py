@@ -158,6 +158,22 @@ def test_skewed_single_expert_many_tiles():
     assert res["ok"], res
 
 
+@pytest.mark.parametrize("T", [8, 31, 32, 33])
+def test_decode_sizes_with_one_full_expert_tile(T):
+    """Calls of at most 32 tokens run the GEMMs' decode layouts (32-row A slots); every token routed
+    to expert 3 fills its tile with T rows, the most those layouts hold (T = 33 is the general path)."""
+    ti = S.token_inputs(T, seed=40 + T)
+    logits = ti.routing_logits.clone()
+    logits[:, 3] = 8.0
+    logits[:, 0:32] += 2.0
+    ti = to_cuda(S.TokenInputs(logits, ti.routing_bias, ti.hidden_states, ti.hidden_states_scale))
+    wb = gpu_bank(32, 0, seed=8)
+    out = _run(ti, wb, 0, 2.5)
+    ref = _gpu_ref(ti, wb, 0, 2.5)
+    res = O.check_tolerance(out, ref)
+    assert res["ok"], res
+
+
 def test_zipf_skewed_load():
     T = 4096
     ti = to_cuda(S.token_inputs(T, seed=9, routing_bias=S.zipf_bias(9)))
