@@ -69,7 +69,8 @@ struct G1Layout {
 // ------------------------------------------------------------------ GEMM2 --
 // Y = C[rows, 2048] . W2[e]^T with C = s * (C_hi + C_lo), N-block = 256 output
 // columns.  Each K step issues two MMAs (hi and lo) into the same accumulator.
-// Epilogue: multiply by the pair's routing weight, store fp32 rows.
+// Epilogue: multiply by the pair's routing weight, store the rows in bf16 (the
+// reduce sums a token's rows in fp32).
 //
 // Two shared-memory layouts.  The general one holds 3 stages of full 128-row hi
 // and lo tiles.  The decode one serves calls with T <= 32 tokens, where no
@@ -429,6 +430,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
+// Two floats rounded to bf16 (nearest even), first in the low half.
+__device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
 // A GEMM2 work unit as the promotion warps see it (tile entry read one unit ahead).
 struct G2Unit {
   int nb2, e, row0, nrows;
@@ -640,27 +647,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       if (live) {
-        // y rows leave through TMA stores: each round the warp writes a 32-row x
-        // 32-column fp32 tile (this lane = one row) into its 128-byte-swizzled
-        // staging buffer, and one lane stores it to y; the buffer is rewritten
-        // only after the previous store has read it.  Rows of the tile beyond
-        // nrows are padding rows of this tile, which nothing reads.
+        // y rows leave in bf16 through TMA stores: each round the warp writes a
+        // 32-row x 64-column tile (this lane = one row, 128 bytes) into its
+        // 128-byte-swizzled staging buffer, and one lane stores it to y; the buffer
+        // is rewritten only after the previous store has read it.  Rows of the
+        // tile beyond nrows are padding rows of this tile, which nothing reads.
         uint8_t* stg = smem + L::OFF_STG + (kDecode ? h : pw) * G2_STG_WARP;
         const int xcol = nb2 * 256 + h * 128;
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
+        for (int m = 0; m < 2; ++m) {
           if (lane == 0) bulk_wait_group_read0();
           __syncwarp();
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const float2 p0 = acc[16 * m + 2 * j], p1 = acc[16 * m + 2 * j + 1];
-            *reinterpret_cast<float4*>(stg + lane * 128 + ((j ^ (lane & 7)) << 4)) =
-                make_float4(p0.x * w, p0.y * w, p1.x * w, p1.y * w);
+            const float2* a = acc + 32 * m + 4 * j;
+            uint4 pk;
+            pk.x = bf16x2_bits(a[0].x * w, a[0].y * w);
+            pk.y = bf16x2_bits(a[1].x * w, a[1].y * w);
+            pk.z = bf16x2_bits(a[2].x * w, a[2].y * w);
+            pk.w = bf16x2_bits(a[3].x * w, a[3].y * w);
+            *reinterpret_cast<uint4*>(stg + lane * 128 + ((j ^ (lane & 7)) << 4)) = pk;
           }
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tm_y, xcol + 32 * m, row0 + q * 32, stg);
+            tma_store_2d(&tm_y, xcol + 64 * m, row0 + q * 32, stg);
             bulk_commit_group();
           }
         }

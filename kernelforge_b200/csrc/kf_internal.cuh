@@ -4,6 +4,7 @@
 #include <cstddef>
 #include <cstdint>
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <utility>
 
@@ -148,7 +149,7 @@ struct PeerOut {
   int rank, world;
 };
 
-cudaError_t launch_reduce(const int32_t* token_slot, const float* y, int T, void* out, int out_fp32, const PeerOut& po,
+cudaError_t launch_reduce(const int32_t* token_slot, const __nv_bfloat16* y, int T, void* out, int out_fp32, const PeerOut& po,
                           int grid, cudaStream_t s);
 
 struct Gemm1Args {
@@ -184,7 +185,7 @@ struct Gemm2Args {
   const float* c_scale;     // [16][p_cap]
   const float* w2_scale;    // [E][56][16]
   const float* slot_weight; // [p_cap]
-  float* y;                 // [p_cap][7168]
+  __nv_bfloat16* y;         // [p_cap][7168]: each row's routing-weighted output, one bf16 rounding
   int32_t p_cap;
   int* status;
   // 1 when the call has at most 32 tokens, so no row tile holds more than 32
@@ -194,7 +195,7 @@ struct Gemm2Args {
 
 cudaError_t launch_gemm1(const CUtensorMap& tm_a, const CUtensorMap& tm_a32, const CUtensorMap& tm_w13,
                          const Gemm1Args& args, int grid, cudaStream_t s);
-// tm_y: fp32 [p_cap, 7168] output rows, box 32 x 32, 128-byte swizzle (TMA stores).
+// tm_y: bf16 [p_cap, 7168] output rows, box 64 x 32, 128-byte swizzle (TMA stores).
 cudaError_t launch_gemm2(const CUtensorMap& tm_chi, const CUtensorMap& tm_clo, const CUtensorMap& tm_chi32,
                          const CUtensorMap& tm_clo32, const CUtensorMap& tm_w2, const CUtensorMap& tm_y,
                          const Gemm2Args& args, int grid, cudaStream_t s);

@@ -97,14 +97,18 @@ int ensure_device(int* num_sms) {
   return d.status;
 }
 
-// Row-major [outer, inner] elements of 1 (u8) or 4 (f32) bytes, box [box_outer, box_inner], 128-byte swizzle.
+// Row-major [outer, inner] elements of 1 (u8), 2 (bf16) or 4 (f32) bytes, box [box_outer, box_inner], 128-byte
+// swizzle.
 bool encode_2d_uncached(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner, uint64_t outer,
                         uint32_t box_inner, uint32_t box_outer) {
   const cuuint64_t dims[2] = {inner, outer};
   const cuuint64_t strides[1] = {inner * static_cast<uint64_t>(elem_bytes)};
   const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t elem_strides[2] = {1, 1};
-  const CUresult r = g_encode(map, elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT8,
+  const CUresult r = g_encode(map,
+                              elem_bytes == 4   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                              : elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                : CU_TENSOR_MAP_DATA_TYPE_UINT8,
                               2, const_cast<void*>(base), dims, strides, box, elem_strides,
                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -242,7 +246,7 @@ int run_experts(const Workspace& w, void* ws, const RowLayout& in, const void* w
   g2.c_scale = g1.c_scale;
   g2.w2_scale = w2_scale;
   g2.slot_weight = ws_ptr<float>(ws, w.slot_weight);
-  g2.y = ws_ptr<float>(ws, w.y);
+  g2.y = ws_ptr<__nv_bfloat16>(ws, w.y);
   g2.p_cap = w.p_cap;
   g2.status = status;
   g2.decode = T <= 32 ? 1 : 0;
@@ -251,7 +255,7 @@ int run_experts(const Workspace& w, void* ws, const RowLayout& in, const void* w
     ProfScope ps(KF_KERNEL_GEMM2, s);
     const int units = w.nt_cap * (kH / 256);
     CUtensorMap tm_y;
-    if (!encode_2d(&tm_y, ws_ptr<float>(ws, w.y), 4, kH, w.p_cap, 32, 32)) return KF_ERR_INVALID_ARGUMENT;
+    if (!encode_2d(&tm_y, ws_ptr<__nv_bfloat16>(ws, w.y), 2, kH, w.p_cap, 64, 32)) return KF_ERR_INVALID_ARGUMENT;
     if (launch_gemm2(tm_chi, tm_clo, tm_chi32, tm_clo32, tm_w2, tm_y, g2, units < num_sms ? units : num_sms, s) !=
         cudaSuccess)
       return KF_ERR_CUDA;
@@ -259,7 +263,7 @@ int run_experts(const Workspace& w, void* ws, const RowLayout& in, const void* w
 
   {
     ProfScope ps(KF_KERNEL_REDUCE, s);
-    if (launch_reduce(ws_ptr<int32_t>(ws, w.token_slot), ws_ptr<float>(ws, w.y), T, out, out_fp32, po, 2 * num_sms,
+    if (launch_reduce(ws_ptr<int32_t>(ws, w.token_slot), ws_ptr<__nv_bfloat16>(ws, w.y), T, out, out_fp32, po, 2 * num_sms,
                       s) !=
         cudaSuccess)
       return KF_ERR_CUDA;
@@ -316,7 +320,7 @@ Workspace plan_workspace(int32_t T, int32_t E) {
   w.c_hi = take(pc * kI);
   w.c_lo = take(pc * kI);
   w.c_scale = take(pc * kIB * 4);
-  w.y = take(pc * kH * 4);
+  w.y = take(pc * kH * 2);  // bf16 rows
   // split-K of GEMM1 for decode-sized calls: with one row tile per active expert
   // its 16 column blocks per tile give about one wave of units, which a 4-way K
   // split turns into four shorter, evenly filled waves

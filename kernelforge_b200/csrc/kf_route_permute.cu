@@ -524,9 +524,9 @@ __global__ void __launch_bounds__(kFrontThreads) front_small_kernel(
   }
 }
 
-// out[t] = sum of the token's permuted rows of y (already routing-weighted), in
-// ascending row order (= ascending local expert, the reference's index_add_ order),
-// accumulated in fp32 from zero and rounded once.  With few tokens (T * 4 or
+// out[t] = sum of the token's permuted rows of y (already routing-weighted and
+// stored in bf16), in ascending row order (= ascending local expert, the
+// reference's index_add_ order), accumulated in fp32 from zero and rounded once.  With few tokens (T * 4 or
 // T * 2 within the grid) 4 or 2 CTAs share each token, one column slice each, so
 // the loads spread over more SMs (T = 16: 9.7 -> 7.6 us).  Each group of CTAs
 // walks its tokens t = group + i * groups in batches of whole tokens with at most
@@ -551,7 +551,7 @@ __device__ __forceinline__ void reduce_store(char* row, bool f32, int c, const f
 }
 
 __global__ void __launch_bounds__(kReduceThreads, 2) unpermute_reduce_kernel(const int32_t* __restrict__ token_slot,
-                                                     const float* __restrict__ y, int T, void* __restrict__ out,
+                                                     const __nv_bfloat16* __restrict__ y, int T, void* __restrict__ out,
                                                      int out_fp32, const PeerOut po, int csplit) {
   grid_dep_wait();
   // Peer return: received row t came from source s (sources in rank order) as the
@@ -639,20 +639,22 @@ __global__ void __launch_bounds__(kReduceThreads, 2) unpermute_reduce_kernel(con
     const int nt = b_tokens;
     const int ne = b_end[nt - 1];
     for (int c = c0 + threadIdx.x; c < c0 + cw; c += kReduceThreads) {
-      float4 v[kReduceBatch];
+      uint2 v[kReduceBatch];  // 4 bf16 columns of each of the batch's rows
 #pragma unroll
       for (int e = 0; e < kReduceBatch; ++e)
-        if (e < ne) v[e] = __ldg(reinterpret_cast<const float4*>(y + static_cast<size_t>(b_slot[e]) * kH) + c);
+        if (e < ne) v[e] = __ldg(reinterpret_cast<const uint2*>(y + static_cast<size_t>(b_slot[e]) * kH) + c);
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
       int j = 0;
       while (j < nt && b_end[j] == 0) reduce_store(b_dst[j++], f32, c, acc);  // tokens without a local row
 #pragma unroll
       for (int e = 0; e < kReduceBatch; ++e) {
         if (e < ne) {
-          acc.x += v[e].x;
-          acc.y += v[e].y;
-          acc.z += v[e].z;
-          acc.w += v[e].w;
+          const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v[e].x));
+          const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v[e].y));
+          acc.x += lo.x;
+          acc.y += lo.y;
+          acc.z += hi.x;
+          acc.w += hi.y;
           while (j < nt && b_end[j] == e + 1) {
             reduce_store(b_dst[j++], f32, c, acc);
             acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -718,7 +720,7 @@ cudaError_t launch_gather_rows(const Meta* meta, const int32_t* tile_rows, const
   return launch_chained(gather_rows_kernel, dim3(grid), dim3(256), 0, s, meta, tile_rows, slot_token, in, p_cap, a_rows, a_scale);
 }
 
-cudaError_t launch_reduce(const int32_t* token_slot, const float* y, int T, void* out, int out_fp32, const PeerOut& po,
+cudaError_t launch_reduce(const int32_t* token_slot, const __nv_bfloat16* y, int T, void* out, int out_fp32, const PeerOut& po,
                           int grid, cudaStream_t s) {
   if (po.peer_back && (po.world < 1 || po.world > kMaxWorld)) return cudaErrorInvalidValue;
   // few tokens: split each token's columns over 2 or 4 CTAs so more SMs share the loads
