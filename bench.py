@@ -522,7 +522,7 @@ def single_gpu_configs(B, S, dev, peaks, bank256) -> dict:
 # only for the kernel source they were captured on: the line reports null once the source changes.
 TRAFFIC = {
     "ep_layer_T8192_per_gpu_256_experts": {
-        "bytes": 8 * (1_230_893_824 + 33_221_888), "source_sha16": "0034b93e9a22f1c9",
+        "bytes": 8 * (1_223_874_560 + 32_855_040), "source_sha16": "8099a11cbb49f7bd",
         "note": "ncu dram__bytes_read.sum + dram__bytes_write.sum of gemm1_swiglu_kernel on a 1/8 replica "
                 "(8192 tokens, 32 local experts: the same pairs per expert), scaled by 8 experts' worth"},
 }
