@@ -526,28 +526,50 @@ __global__ void __launch_bounds__(kFrontThreads) front_small_kernel(
 
 // out[t] = sum of the token's permuted rows of y (already routing-weighted and
 // stored in bf16), in ascending row order (= ascending local expert, the
-// reference's index_add_ order), accumulated in fp32 from zero and rounded once.  With few tokens (T * 4 or
-// T * 2 within the grid) 4 or 2 CTAs share each token, one column slice each, so
-// the loads spread over more SMs (T = 16: 9.7 -> 7.6 us).  Each group of CTAs
-// walks its tokens t = group + i * groups in batches of whole tokens with at most
-// kReduceBatch rows between them: warp 0 lists a batch's rows and output rows in
-// shared memory, then each thread loads its 4 columns of every row of the batch
-// at once and sums them token by token.  So a call whose tokens have one local
-// row each (a GPU holding 32 of the 256 experts) keeps as many loads in flight as
-// one whose tokens have eight.
-constexpr int kReduceThreads = 448;   // 14 warps: a row's 1792 float4 columns in 4 passes
+// reference's index_add_ order), accumulated in fp32 from zero and rounded
+// once.  With few tokens (T * 4 or T * 2 within the grid) 4 or 2 CTAs share each
+// token, one column slice each, so the loads spread over more SMs (T = 16:
+// 9.7 -> 7.6 us).  Each group of CTAs walks its tokens t = group + i * groups in
+// batches of whole tokens with at most kReduceBatch rows between them: warp 0
+// lists a batch's rows and output rows in shared memory, then each thread loads
+// its 8 columns (16 bytes of bf16) of every row of the batch at once and sums
+// them token by token.  So a call whose tokens have one local row each (a GPU
+// holding 32 of the 256 experts) keeps as many loads in flight as one whose
+// tokens have eight.
+constexpr int kReduceThreads = 448;   // 14 warps: a row's 896 groups of 8 columns in 2 passes
 constexpr int kReduceBatch = 8;       // rows of y per batch (a token has at most 8)
 constexpr int kMaxWorld = 64;
 
-__device__ __forceinline__ void reduce_store(char* row, bool f32, int c, const float4& v) {
+__device__ __forceinline__ uint32_t bf16x2_word(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// Columns 8c .. 8c+7 of an output row: one 16-byte bf16 store, or two fp32 ones.
+__device__ __forceinline__ void reduce_store(char* row, bool f32, int c, const float4& a, const float4& b) {
   if (!row) return;
   if (f32) {
-    reinterpret_cast<float4*>(row)[c] = v;
+    reinterpret_cast<float4*>(row)[2 * c] = a;
+    reinterpret_cast<float4*>(row)[2 * c + 1] = b;
   } else {
-    const __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
-    reinterpret_cast<uint2*>(row)[c] =
-        make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+    reinterpret_cast<uint4*>(row)[c] =
+        make_uint4(bf16x2_word(a.x, a.y), bf16x2_word(a.z, a.w), bf16x2_word(b.x, b.y), bf16x2_word(b.z, b.w));
   }
+}
+
+__device__ __forceinline__ void add_bf16x8(float4& a, float4& b, const uint4& v) {
+  const float2 p0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.x));
+  const float2 p1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.y));
+  const float2 p2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.z));
+  const float2 p3 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v.w));
+  a.x += p0.x;
+  a.y += p0.y;
+  a.z += p1.x;
+  a.w += p1.y;
+  b.x += p2.x;
+  b.y += p2.y;
+  b.z += p3.x;
+  b.w += p3.y;
 }
 
 __global__ void __launch_bounds__(kReduceThreads, 2) unpermute_reduce_kernel(const int32_t* __restrict__ token_slot,
@@ -588,7 +610,7 @@ __global__ void __launch_bounds__(kReduceThreads, 2) unpermute_reduce_kernel(con
   const bool f32 = out_fp32 && !po.peer_back;
   // csplit CTAs share each token, one slice of kH / csplit columns each
   const int cta = static_cast<int>(blockIdx.x) / csplit, ncta = static_cast<int>(gridDim.x) / csplit;
-  const int cw = kH / 4 / csplit, c0 = (static_cast<int>(blockIdx.x) % csplit) * cw;
+  const int cw = kH / 8 / csplit, c0 = (static_cast<int>(blockIdx.x) % csplit) * cw;  // groups of 8 columns
   const int ntok = cta < T ? (T - 1 - cta) / ncta + 1 : 0;
   for (int i0 = 0; i0 < ntok;) {
     if (warp == 0) {
@@ -639,25 +661,21 @@ __global__ void __launch_bounds__(kReduceThreads, 2) unpermute_reduce_kernel(con
     const int nt = b_tokens;
     const int ne = b_end[nt - 1];
     for (int c = c0 + threadIdx.x; c < c0 + cw; c += kReduceThreads) {
-      uint2 v[kReduceBatch];  // 4 bf16 columns of each of the batch's rows
+      uint4 v[kReduceBatch];  // 8 bf16 columns of each of the batch's rows
 #pragma unroll
       for (int e = 0; e < kReduceBatch; ++e)
-        if (e < ne) v[e] = __ldg(reinterpret_cast<const uint2*>(y + static_cast<size_t>(b_slot[e]) * kH) + c);
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (e < ne) v[e] = __ldg(reinterpret_cast<const uint4*>(y + static_cast<size_t>(b_slot[e]) * kH) + c);
+      float4 acc0 = make_float4(0.f, 0.f, 0.f, 0.f), acc1 = acc0;
       int j = 0;
-      while (j < nt && b_end[j] == 0) reduce_store(b_dst[j++], f32, c, acc);  // tokens without a local row
+      while (j < nt && b_end[j] == 0) reduce_store(b_dst[j++], f32, c, acc0, acc1);  // tokens without a local row
 #pragma unroll
       for (int e = 0; e < kReduceBatch; ++e) {
         if (e < ne) {
-          const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v[e].x));
-          const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v[e].y));
-          acc.x += lo.x;
-          acc.y += lo.y;
-          acc.z += hi.x;
-          acc.w += hi.y;
+          add_bf16x8(acc0, acc1, v[e]);
           while (j < nt && b_end[j] == e + 1) {
-            reduce_store(b_dst[j++], f32, c, acc);
-            acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            reduce_store(b_dst[j++], f32, c, acc0, acc1);
+            acc0 = make_float4(0.f, 0.f, 0.f, 0.f);
+            acc1 = acc0;
           }
         }
       }
