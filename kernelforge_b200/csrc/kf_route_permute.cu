@@ -347,8 +347,10 @@ __global__ void __launch_bounds__(256) permute_assign_kernel(
 }
 
 // Copies each permuted row's FP8 hidden row (7168 bytes) and its 56 scales into
-// the expert-contiguous A buffer.  One warp per row, grid-strided over all row
-// tiles so every SM streams; padding rows of a tile are skipped.
+// the expert-contiguous A buffer.  Rows: one warp per row, grid-strided over all
+// row tiles so every SM streams; padding rows of a tile are skipped.  Scales: one
+// warp per 32 consecutive rows, so the K-block-major scale array is written in
+// whole 128-byte runs.
 __global__ void __launch_bounds__(256) gather_rows_kernel(const Meta* __restrict__ meta,
                                                           const int32_t* __restrict__ tile_rows,
                                                           const int32_t* __restrict__ slot_token,
@@ -358,21 +360,40 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const Meta* __restrict
   grid_dep_wait();
   const int lane = threadIdx.x & 31;
   const int warps = blockDim.x >> 5;
+  const int gw = blockIdx.x * warps + (threadIdx.x >> 5), nw = gridDim.x * warps;
+  // the rows: one warp per row, every load of the row issued before the first store
   const int nrows = meta->num_tiles * kBlk;
-  for (int r = blockIdx.x * warps + (threadIdx.x >> 5); r < nrows; r += gridDim.x * warps) {
+  for (int r = gw; r < nrows; r += nw) {
     if ((r & (kBlk - 1)) >= tile_rows[r >> 7]) continue;
     const int t = slot_token[r];
     const uint4* src = reinterpret_cast<const uint4*>(in.row(t));
     uint4* dst = reinterpret_cast<uint4*>(a_rows + static_cast<size_t>(r) * kH);
-    // every load of the row and its scales is issued before the first store
     uint4 v[kH / 16 / 32];
 #pragma unroll
     for (int j = 0; j < kH / 16 / 32; ++j) v[j] = src[lane + 32 * j];
-    const float sc0 = in.sc(t, lane), sc1 = lane + 32 < kHB ? in.sc(t, lane + 32) : 0.f;
 #pragma unroll
     for (int j = 0; j < kH / 16 / 32; ++j) dst[lane + 32 * j] = v[j];
-    a_scale[static_cast<size_t>(lane) * p_cap + r] = sc0;
-    if (lane + 32 < kHB) a_scale[static_cast<size_t>(lane + 32) * p_cap + r] = sc1;
+  }
+  // the scales ([56][p_cap], K-block-major): one warp per 32 consecutive rows, lane
+  // = row, so each of a warp's stores fills 128 contiguous bytes (one store per row
+  // and K block would write 56 separate sectors per row)
+  const int nblk = meta->num_tiles * (kBlk / 32);
+  for (int b = gw; b < nblk; b += nw) {
+    const int rb = b * 32;
+    const int n = tile_rows[rb >> 7] - (rb & (kBlk - 1));  // real rows in this block (<= 0: none)
+    if (n <= 0) continue;
+    const bool live = lane < n;
+    const int t = live ? slot_token[rb + lane] : 0;
+    float* dst = a_scale + rb + lane;
+#pragma unroll
+    for (int kb0 = 0; kb0 < kHB; kb0 += 8) {
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = live ? in.sc(t, kb0 + i) : 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (live) dst[static_cast<size_t>(kb0 + i) * p_cap] = v[i];
+    }
   }
 }
 
